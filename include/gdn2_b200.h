@@ -1,0 +1,131 @@
+/*
+ * gdn2_b200.h -- C ABI of the B200 (sm_100a) Gated DeltaNet-2 operator.
+ *
+ * This is the drop-in boundary for the reference operator
+ *   make_blr_trainable(cfg, scale)(q, k, v, w, b, g, h0) -> (o, h_final)
+ * of atomic_gdn2 (atomic_gdn2/pipeline.py:17-66), whose forward is the three
+ * Pallas kernels build_scores / wy_solve_leafbatched / recompute_and_scan_slim
+ * (pipeline.py:20-26) and whose backward is backward_mega (pipeline.py:38-47,
+ * bwd/mega.py:61-79).  gdn2_fwd replaces `core_fwd` (pipeline.py:33-36) for one
+ * segment, gdn2_bwd replaces `core_bwd` (pipeline.py:38-47).
+ *
+ * Plain C: raw device pointers, sizes and a CUDA stream (passed as void*).
+ * Every buffer is allocated by the caller; the library owns no device memory.
+ *
+ * Layout: q, k, v, w, b, g, o, d_o and the six input gradients are (B, H, L, D)
+ * tensors with unit stride along D, row stride D along L, and element strides
+ * stride_b / stride_h along B / H (so segment views of a longer sequence need no
+ * copy).  h0, h_final, d_hfinal and dh0 are contiguous (B, H, D, D) fp32 with
+ * index [b][h][d_k][d_v].  o and h_final are fp32 (the reference returns the f32
+ * kernel output, fwd/cd_slim.py:45); the six gradients are written in in_dtype
+ * after the reference's final sanitize at 1e4 (pipeline.py:11-14, 44-47).
+ */
+#ifndef GDN2_B200_H
+#define GDN2_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum gdn2_status {
+  GDN2_OK = 0,
+  /* Shape / dtype / config rejected before any launch.  Mirrors the reference's
+   * ValueError paths (config.py:52-65, pipeline.py:54-55). */
+  GDN2_ERR_INVALID_ARGUMENT = 1,
+  /* A CUDA runtime call (launch, attribute set) failed. */
+  GDN2_ERR_CUDA = 2,
+  /* A configuration the reference accepts but this build does not implement. */
+  GDN2_ERR_UNSUPPORTED = 3
+} gdn2_status;
+
+/* Dot-product precision modes (precision.py:8-37 plus one extra):
+ *   HIGHEST  fp32-class products: 3 x tf32 (hi*hi + hi*lo + lo*hi)
+ *   BF16X3   3 x bf16, the reference's dot_bf16x3 (precision.py:14-17)
+ *   DEFAULT  1 x bf16 (jnp.dot at Precision.DEFAULT)
+ *   TF32     1 x tf32 (no counterpart in the reference) */
+typedef enum gdn2_precision {
+  GDN2_PREC_HIGHEST = 0,
+  GDN2_PREC_BF16X3 = 1,
+  GDN2_PREC_DEFAULT = 2,
+  GDN2_PREC_TF32 = 3
+} gdn2_precision;
+
+typedef enum gdn2_dtype { GDN2_F32 = 0, GDN2_BF16 = 1 } gdn2_dtype;
+
+/* Bits of the device status word the kernels OR into (read it after the stream
+ * has been synchronised). */
+#define GDN2_DEV_TIMEOUT 1u        /* a bounded on-chip wait ran out (results invalid) */
+#define GDN2_DEV_SPAN 2u           /* a chunk's per-channel gate span exceeds the supported range */
+#define GDN2_DEV_POSITIVE_GATE 4u  /* g > 0 seen: outside domain I-1 (domain.py:1-6) */
+
+/* Operator descriptor.  Fields mirror BLRConfig (config.py:28-50) where they
+ * affect the arithmetic; TPU tiling fields are not part of the ABI. */
+typedef struct gdn2_desc {
+  int32_t B, H, L, D;        /* L % bt == 0 (pipeline.py:54-55); D == 128 */
+  int64_t stride_b;          /* element stride between batches of the (B,H,L,D) tensors */
+  int64_t stride_h;          /* element stride between heads */
+  int32_t bt;                /* chunk length, 128 */
+  float scale;               /* output scale (make_blr_trainable's `scale`) */
+  float wy_eps;              /* WY damping: A = (I + (1 - wy_eps) Akk)^-1 (fwd/solve.py:21-28) */
+  float clip;                /* sanitize bound of intermediates (precision.py:50-51) */
+  int32_t dot_mode;          /* gdn2_precision for scores / recompute / scan / B5 */
+  int32_t solve_dot_mode;    /* gdn2_precision for the WY solve products */
+  int32_t b3_dot_mode;       /* gdn2_precision for backward stages B1-B3 */
+  int32_t in_dtype;          /* gdn2_dtype of q..g and of the six gradients */
+} gdn2_desc;
+
+/* Bytes of the residual buffer gdn2_fwd fills and gdn2_bwd reads for one call
+ * (forward intermediates: scores, WY inverse, per-chunk states, ...). */
+size_t gdn2_residual_bytes(const gdn2_desc* desc);
+
+/* Bytes of scratch gdn2_bwd needs beyond the residual buffer. */
+size_t gdn2_bwd_workspace_bytes(const gdn2_desc* desc);
+
+/* Forward over all L/bt chunks of one segment.  Replaces core_fwd
+ * (pipeline.py:33-36 -> _fwd :20-26): gate cumsum, scores, WY solve,
+ * recompute and the inter-chunk state scan.
+ *   h0        (B,H,D,D) fp32 initial state, or NULL for zeros (pipeline.py:57)
+ *   o         (B,H,L,D) fp32 output
+ *   h_final   (B,H,D,D) fp32 final state
+ *   residual  gdn2_residual_bytes(desc) bytes, 256-byte aligned
+ *   dev_status device uint32 the kernels OR status bits into (caller zeroes it)
+ *   stream    cudaStream_t */
+gdn2_status gdn2_fwd(const gdn2_desc* desc, const void* q, const void* k, const void* v, const void* w,
+                     const void* b, const void* g, const float* h0, float* o, float* h_final, void* residual,
+                     uint32_t* dev_status, void* stream);
+
+/* Backward of one segment.  Replaces core_bwd (pipeline.py:38-47 ->
+ * backward_mega, bwd/mega.py:61-79).
+ *   residual  the buffer gdn2_fwd filled for the same inputs
+ *   d_o       (B,H,L,D) fp32 cotangent of o (the reference casts do to f32, pipeline.py:42)
+ *   d_hfinal  (B,H,D,D) fp32 cotangent of h_final, or NULL for zeros
+ *   dq..dg    (B,H,L,D) gradients in in_dtype
+ *   dh0       (B,H,D,D) fp32 gradient of h0
+ *   workspace gdn2_bwd_workspace_bytes(desc) bytes, 256-byte aligned */
+gdn2_status gdn2_bwd(const gdn2_desc* desc, const void* q, const void* k, const void* v, const void* w,
+                     const void* b, const void* g, const void* residual, const float* d_o, const float* d_hfinal,
+                     void* dq, void* dk, void* dv, void* dw, void* db, void* dg, float* dh0, void* workspace,
+                     uint32_t* dev_status, void* stream);
+
+/* Human-readable name of a status code (static string). */
+const char* gdn2_status_string(gdn2_status status);
+
+/* Library self-test hook (no counterpart in the reference): one 128 x N x 128
+ * tensor-core GEMM through the same shared-memory operand path the operator
+ * kernels use.  C[m][n] = sum_k A'[m][k] B[k][n] with A' = A, or A' = A^T when
+ * a_mode == 3.  A, B, C are contiguous fp32 device arrays (A 128x128, B 128xN,
+ * C 128xN).  a_mode: 0 K-major slices, 1 MN-major slices, 2 whole-K K-major tile,
+ * 3 whole-K K-major tile read through the transposed (MN-major) view (bf16 modes
+ * only; tf32 returns GDN2_ERR_UNSUPPORTED).
+ * b_mn: 0 K-major, 1 MN-major.  N in {32, 64, 128, 256}. */
+gdn2_status gdn2_selftest_gemm(const float* A, const float* B, float* C, int32_t N, int32_t precision,
+                               int32_t a_mode, int32_t b_mn, uint32_t* dev_status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GDN2_B200_H */
