@@ -1,0 +1,216 @@
+"""The differentiable operator: make_blr_trainable(cfg, scale)(q, k, v, w, b, g, h0) -> (o, h_final).
+
+Drop-in for atomic_gdn2/pipeline.py:17-66 (make_blr_trainable / call) with PyTorch autograd in
+place of jax.custom_vjp:
+
+* inputs q..g are (B, H, L, D) tensors of one float dtype on a CUDA device; L % cfg.bt == 0 or
+  ValueError (pipeline.py:54-55); h0 is (B, H, D, D) fp32 or None for zeros (pipeline.py:57);
+* o and h_final are fp32 (pipeline.py:45 returns the f32 kernel output);
+* long sequences are processed in segments of cfg.max_chunks_per_call chunks that carry h
+  (pipeline.py:59-64); the whole call is one autograd node, the per-segment launches write into
+  strided views of one output, so there is no concatenation copy;
+* backward returns gradients for all seven arguments, each in its input's dtype after the final
+  sanitize at 1e4 (pipeline.py:11-14, 38-47); do and dh_final are taken as fp32 (pipeline.py:42).
+
+All arithmetic runs in libgdn2_b200.so (hand-written sm_100a kernels) through the C ABI of
+include/gdn2_b200.h.  PyTorch only provides device memory, streams and autograd plumbing.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+
+from . import _lib
+from .config import BLRConfig
+
+_FINAL_CLIP = 1e4
+_checks = os.environ.get("GDN2_CHECK", "1") != "0"
+
+
+def set_checks(enabled: bool) -> None:
+    """Synchronise after every launch and turn device status bits into exceptions (default on;
+    environment GDN2_CHECK=0 turns it off).  With checks off, read `last_status()` yourself."""
+    global _checks
+    _checks = bool(enabled)
+
+
+_last_status: torch.Tensor | None = None
+
+
+def last_status() -> int:
+    """Device status bits of the most recent call (synchronises)."""
+    return 0 if _last_status is None else int(_last_status.item())
+
+
+def _raise_on_status(st: torch.Tensor, what: str):
+    code = int(st.item())
+    if code == 0:
+        return
+    msgs = []
+    if code & _lib.DEV_TIMEOUT:
+        msgs.append("an on-chip wait timed out (results invalid)")
+    if code & _lib.DEV_SPAN:
+        msgs.append("a chunk's per-channel gate span exceeds the supported range "
+                    "(sum of |g| over one chunk > 128); clamp g (domain.clamp_g) or shorten bt")
+    if code & _lib.DEV_POSITIVE_GATE:
+        msgs.append("g > 0 seen: outside domain I-1 (g <= 0)")
+    raise RuntimeError(f"{what}: " + "; ".join(msgs))
+
+
+def _ptr(t):
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+class _Segment:
+    """Static description of one segment launch: chunk range and C descriptor."""
+
+    def __init__(self, desc: _lib.Gdn2Desc, a: int, c: int):
+        self.desc, self.a, self.c = desc, a, c
+
+
+def _make_desc(cfg: BLRConfig, scale: float, B, H, Lseg, D, stride_b, stride_h, dtype) -> _lib.Gdn2Desc:
+    d = _lib.Gdn2Desc()
+    d.B, d.H, d.L, d.D = B, H, Lseg, D
+    d.stride_b, d.stride_h = stride_b, stride_h
+    d.bt = cfg.bt
+    d.scale, d.wy_eps, d.clip = float(scale), float(cfg.wy_eps), float(cfg.clip)
+    d.dot_mode = _lib.PREC[cfg.dot_mode]
+    d.solve_dot_mode = _lib.PREC[cfg.solve_dot_mode]
+    d.b3_dot_mode = _lib.PREC[cfg.b3_dot_mode]
+    d.in_dtype = _lib.BF16 if dtype == torch.bfloat16 else _lib.F32
+    return d
+
+
+def _fin(x: torch.Tensor, dt: torch.dtype, cfg: BLRConfig) -> torch.Tensor:
+    """pipeline.py:11-14: the kernels already sanitize at cfg.clip and write in the input dtype;
+    re-sanitize only when cfg.clip is looser than the final 1e4 bound."""
+    if cfg.clip <= _FINAL_CLIP and x.dtype == dt:
+        return x
+    return torch.nan_to_num(x.float().clamp(-_FINAL_CLIP, _FINAL_CLIP), nan=0.0,
+                            posinf=_FINAL_CLIP, neginf=-_FINAL_CLIP).to(dt)
+
+
+class _GDN2(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, cfg, scale, need_res, q, k, v, w, b, g, h0):
+        lib = _lib.load()
+        B, H, L, D = q.shape
+        dev = q.device
+        nc = L // cfg.bt
+        seg = cfg.max_chunks_per_call
+        o = torch.empty((B, H, L, D), dtype=torch.float32, device=dev)
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+        h = h0
+        segments, residuals = [], []
+        for s in range(0, nc, seg):
+            e = min(nc, s + seg)
+            a = s * cfg.bt
+            desc = _make_desc(cfg, scale, B, H, (e - s) * cfg.bt, D, q.stride(0), q.stride(1), q.dtype)
+            nbytes = lib.gdn2_residual_bytes(ctypes.byref(desc))
+            if nbytes == 0:
+                _lib.check(_lib.ERR_INVALID_ARGUMENT, "gdn2_residual_bytes")
+            res = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+            h_out = torch.empty((B, H, D, D), dtype=torch.float32, device=dev)
+            off = a * D
+            el = q.element_size()
+            ins = [ctypes.c_void_p(t.data_ptr() + off * el) for t in (q, k, v, w, b, g)]
+            rc = lib.gdn2_fwd(ctypes.byref(desc), *ins, _ptr(h), ctypes.c_void_p(o.data_ptr() + off * 4),
+                              _ptr(h_out), _ptr(res), _ptr(status), _stream())
+            _lib.check(rc, "gdn2_fwd")
+            segments.append(_Segment(desc, s, e))
+            residuals.append(res if need_res else None)
+            h = h_out
+        global _last_status
+        _last_status = status
+        if _checks:
+            _raise_on_status(status, "gdn2_fwd")
+        ctx.cfg, ctx.segments = cfg, segments
+        ctx.h0_dtype = None if h0 is None else h0.dtype
+        ctx.residuals = residuals
+        ctx.save_for_backward(q, k, v, w, b, g)
+        return o, h
+
+    @staticmethod
+    def backward(ctx, do, dhf):
+        lib = _lib.load()
+        cfg = ctx.cfg
+        q, k, v, w, b, g = ctx.saved_tensors
+        B, H, L, D = q.shape
+        dev = q.device
+        if any(r is None for r in ctx.residuals):
+            raise RuntimeError("gdn2: backward through a call made without gradient tracking")
+        do = (torch.zeros((B, H, L, D), dtype=torch.float32, device=dev) if do is None
+              else do.to(torch.float32))
+        if do.stride(-1) != 1 or do.stride(-2) != D or do.stride(0) != q.stride(0) or do.stride(1) != q.stride(1):
+            do = do.contiguous()
+            if do.stride(0) != q.stride(0) or do.stride(1) != q.stride(1):
+                raise RuntimeError("gdn2: cotangent layout does not match the inputs")
+        dh = None if dhf is None else dhf.to(torch.float32).contiguous()
+        grads = [torch.empty_like(t) for t in (q, k, v, w, b, g)]
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+        el = q.element_size()
+        for sgm, res in zip(reversed(ctx.segments), reversed(ctx.residuals)):
+            off = sgm.a * cfg.bt * D
+            ws = torch.empty(lib.gdn2_bwd_workspace_bytes(ctypes.byref(sgm.desc)), dtype=torch.uint8, device=dev)
+            dh0 = torch.empty((B, H, D, D), dtype=torch.float32, device=dev)
+            ins = [ctypes.c_void_p(t.data_ptr() + off * el) for t in (q, k, v, w, b, g)]
+            outs = [ctypes.c_void_p(t.data_ptr() + off * el) for t in grads]
+            rc = lib.gdn2_bwd(ctypes.byref(sgm.desc), *ins, _ptr(res), ctypes.c_void_p(do.data_ptr() + off * 4),
+                              _ptr(dh), *outs, _ptr(dh0), _ptr(ws), _ptr(status), _stream())
+            _lib.check(rc, "gdn2_bwd")
+            dh = dh0
+        global _last_status
+        _last_status = status
+        if _checks:
+            _raise_on_status(status, "gdn2_bwd")
+        grads = [_fin(gr, t.dtype, cfg) for gr, t in zip(grads, (q, k, v, w, b, g))]
+        dh0 = None
+        if ctx.h0_dtype is not None and ctx.needs_input_grad[9]:
+            dh0 = _fin(dh, ctx.h0_dtype, cfg)
+        return (None, None, None, *grads, dh0)
+
+
+def _prep(ts):
+    """Common dtype and row-contiguous layout for the six (B,H,L,D) inputs."""
+    dts = {t.dtype for t in ts}
+    dt = dts.pop() if len(dts) == 1 else torch.float32
+    if dt not in (torch.float32, torch.bfloat16):
+        dt = torch.float32
+    ts = [t.to(dt) for t in ts]
+    D = ts[0].shape[-1]
+    s0 = ts[0].stride()
+    if any(t.stride(-1) != 1 or t.stride(-2) != D for t in ts) or any(t.stride() != s0 for t in ts):
+        ts = [t.contiguous() for t in ts]
+    return ts
+
+
+def make_blr_trainable(cfg: BLRConfig, scale):
+    """pipeline.py:17: returns call(q, k, v, w, b, g, h0=None) -> (o, h_final)."""
+    scale = float(scale)
+
+    def call(q, k, v, w, b, g, h0=None):
+        """q..g: (B,H,L,D), L % bt == 0.  Returns (o (B,H,L,D) fp32, h_final (B,H,D,D) fp32)."""
+        bsz, H, L, D = q.shape
+        if L % cfg.bt:
+            raise ValueError(f"L={L} must be divisible by bt={cfg.bt}")
+        for t in (k, v, w, b, g):
+            if t.shape != q.shape:
+                raise ValueError(f"all of q, k, v, w, b, g must have shape {tuple(q.shape)}")
+        if not q.is_cuda:
+            raise RuntimeError("gdn2: inputs must be CUDA tensors (the operator runs only on the B200 kernels)")
+        if h0 is not None:
+            if h0.shape != (bsz, H, D, D):
+                raise ValueError(f"h0 must have shape {(bsz, H, D, D)}")
+            h0 = h0.to(torch.float32).contiguous()
+        xs = _prep([q, k, v, w, b, g])
+        need_res = torch.is_grad_enabled() and (any(t.requires_grad for t in xs)
+                                                or (h0 is not None and h0.requires_grad))
+        return _GDN2.apply(cfg, scale, need_res, *xs, h0)
+
+    return call

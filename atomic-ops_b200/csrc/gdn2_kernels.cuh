@@ -1,0 +1,225 @@
+// Kernel parameter blocks, the residual / workspace layout, and the small CTA-level helpers
+// shared by the forward and backward kernels.
+#pragma once
+
+#include "gdn2_common.cuh"
+
+namespace gdn2 {
+
+// Largest per-channel gate span (max_t gc - min_t gc inside one chunk) the single-reference
+// factorisation accepts: every exponential leg stays within e^(+-kSpanMax/2), far inside the
+// fp32 normal range, so hi/lo splits of the legs stay exact.
+constexpr float kSpanMax = 128.0f;
+
+// Bytes of one encoded 128x128 operand image (one precision part) for a mode.
+__host__ __device__ inline uint32_t image_part_bytes(Mode m) { return m.fmt == kTF32 ? 65536u : 32768u; }
+__host__ __device__ inline uint32_t image_bytes(Mode m) { return image_part_bytes(m) * (m.passes == 3 ? 2u : 1u); }
+
+// Per-call residual layout (byte offsets from the residual base), all regions 256-byte aligned.
+struct ResLayout {
+  size_t aqk, ainv, wp, u, mf, mb, bc, hs, vnew, total;
+  uint32_t mf_stride, mb_stride;  // bytes per chunk-head of the two state-transition images
+};
+
+__host__ __device__ inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+__host__ __device__ inline ResLayout res_layout(int BH, int NC, Mode fwd_scan, Mode bwd_scan) {
+  ResLayout r{};
+  const size_t nch = (size_t)BH * NC;
+  const size_t mat = (size_t)kT * kD * 4;  // one 128x128 fp32 matrix
+  size_t o = 0;
+  r.aqk = o; o = align256(o + nch * mat);
+  r.ainv = o; o = align256(o + nch * mat);
+  r.wp = o; o = align256(o + nch * mat);
+  r.u = o; o = align256(o + nch * mat);
+  r.mf_stride = image_bytes(fwd_scan);
+  r.mb_stride = image_bytes(bwd_scan);
+  r.mf = o; o = align256(o + nch * r.mf_stride);
+  r.mb = o; o = align256(o + nch * r.mb_stride);
+  r.bc = o; o = align256(o + nch * mat);
+  r.hs = o; o = align256(o + (size_t)BH * (NC + 1) * mat);  // h entering each chunk, then h_final
+  r.vnew = o; o = align256(o + nch * mat);
+  r.total = o;
+  return r;
+}
+
+// Backward workspace layout.
+struct WsLayout {
+  size_t dvl, cc, dhs, total;
+};
+__host__ __device__ inline WsLayout ws_layout(int BH, int NC) {
+  WsLayout w{};
+  const size_t nch = (size_t)BH * NC;
+  const size_t mat = (size_t)kT * kD * 4;
+  size_t o = 0;
+  w.dvl = o; o = align256(o + nch * mat);
+  w.cc = o; o = align256(o + nch * mat);
+  w.dhs = o; o = align256(o + nch * mat);  // dh entering each chunk from the right
+  w.total = o;
+  return w;
+}
+
+struct OpParams {
+  const void* q; const void* k; const void* v; const void* w; const void* b; const void* g;
+  long long stride_b, stride_h;  // elements
+  int H, NC;                     // heads, chunks in this call
+  float scale, eps, clip;
+  int dot_mode, solve_mode, b3_mode;
+  unsigned* status;
+  uint8_t* res;                  // residual base
+  ResLayout rl;
+};
+
+// Element offset of chunk c of head (b, h) in a (B,H,L,D) tensor.
+__device__ __forceinline__ long long chunk_off(const OpParams& p, int bh, int c) {
+  const int b = bh / p.H, h = bh % p.H;
+  return (long long)b * p.stride_b + (long long)h * p.stride_h + (long long)c * kT * kD;
+}
+
+// ---------------------------------------------------------------------------
+// CTA helpers for the "stage -> issue -> wait" rhythm (single-buffered operand pool)
+// ---------------------------------------------------------------------------
+// Make the staged operands visible to the tensor core and order prior TMEM accesses.
+__device__ __forceinline__ void staged_sync() {
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+}
+
+struct MmaBar {
+  uint64_t* bar;
+  uint32_t phase;
+  unsigned* status;
+  __device__ __forceinline__ void commit_wait() {
+    if (threadIdx.x == 0) mma_commit(bar);
+    mbar_wait(bar, phase, status);
+    phase ^= 1u;
+    tc_fence_after();
+  }
+};
+
+// Element size in bytes and K elements per 128-byte slice.
+__device__ __forceinline__ int esize(Mode m) { return m.fmt == kTF32 ? 4 : 2; }
+__device__ __forceinline__ int kslice(Mode m) { return m.fmt == kTF32 ? 32 : 64; }
+
+// Operand pool: tile i is 16 KB at base + i * 16 KB.
+__device__ __forceinline__ Tile pool_k(uint32_t base, int i) { return tile_k(base + (uint32_t)i * 16384u, 128); }
+__device__ __forceinline__ Tile pool_mn(uint32_t base, int i, Mode m) {
+  return tile_mn(base + (uint32_t)i * 16384u, 128u * (uint32_t)esize(m), m.fmt);
+}
+
+// Issue one K-slice (4 MMA K-steps) for operand pairs stored in pool tiles.
+__device__ __forceinline__ void issue_slice(Mode m, uint32_t dcol, const Tile a[2], const Tile b[2], int N,
+                                            bool neg_a, bool accumulate) {
+  mma_tiles(m.fmt, m.passes, dcol, a, b, N, 4, neg_a, accumulate);
+}
+
+// Write one value of an encoded image (hi/lo parts) of a 128x128 matrix in the K-major
+// whole-K layout: element (row, col).  `dst` is the image base (hi part; lo part follows).
+__device__ __forceinline__ uint32_t image_offset(Mode m, int row, int col) {
+  const uint32_t e = (uint32_t)esize(m);
+  const uint32_t kb = (uint32_t)col * e;
+  const uint32_t sbo = 8u * 128u * e;
+  return ((uint32_t)row >> 3) * sbo + (kb >> 4) * 128u + ((uint32_t)row & 7u) * 16u + (kb & 15u);
+}
+
+// Encode 8 consecutive values of row `row` (cols c0..c0+7) of a matrix into a K-major
+// whole-K image in global memory (16-byte stores for bf16, two 16-byte stores for tf32).
+__device__ __forceinline__ void image_store8(uint8_t* dst, Mode m, int row, int c0, const float v[8]) {
+  const uint32_t part = image_part_bytes(m);
+  if (m.fmt == kTF32) {
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      uint4 hi, lo;
+      uint32_t* ph = reinterpret_cast<uint32_t*>(&hi);
+      uint32_t* pl = reinterpret_cast<uint32_t*>(&lo);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float x = v[4 * hh + i];
+        ph[i] = tf32_rna(x);
+        pl[i] = tf32_rna(x - __uint_as_float(ph[i]));
+      }
+      const uint32_t off = image_offset(m, row, c0 + 4 * hh);
+      *reinterpret_cast<uint4*>(dst + off) = hi;
+      if (m.passes == 3) *reinterpret_cast<uint4*>(dst + part + off) = lo;
+    }
+  } else {
+    uint4 hi, lo;
+    uint32_t* ph = reinterpret_cast<uint32_t*>(&hi);
+    uint32_t* pl = reinterpret_cast<uint32_t*>(&lo);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __nv_bfloat162 hv = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+      float2 hf = __bfloat1622float2(hv);
+      __nv_bfloat162 lv = __floats2bfloat162_rn(v[2 * i] - hf.x, v[2 * i + 1] - hf.y);
+      ph[i] = *reinterpret_cast<uint32_t*>(&hv);
+      pl[i] = *reinterpret_cast<uint32_t*>(&lv);
+    }
+    const uint32_t off = image_offset(m, row, c0);
+    *reinterpret_cast<uint4*>(dst + off) = hi;
+    if (m.passes == 3) *reinterpret_cast<uint4*>(dst + part + off) = lo;
+  }
+}
+
+// Encode one scalar at (row, col) of an image (used to write a transpose from row owners).
+__device__ __forceinline__ void image_store1(uint8_t* dst, Mode m, int row, int col, float x) {
+  const uint32_t part = image_part_bytes(m);
+  const uint32_t off = image_offset(m, row, col);
+  if (m.fmt == kTF32) {
+    const uint32_t h = tf32_rna(x);
+    *reinterpret_cast<uint32_t*>(dst + off) = h;
+    if (m.passes == 3) *reinterpret_cast<uint32_t*>(dst + part + off) = tf32_rna(x - __uint_as_float(h));
+  } else {
+    const __nv_bfloat16 h = __float2bfloat16_rn(x);
+    *reinterpret_cast<__nv_bfloat16*>(dst + off) = h;
+    if (m.passes == 3) *reinterpret_cast<__nv_bfloat16*>(dst + part + off) = __float2bfloat16_rn(x - __bfloat162float(h));
+  }
+}
+
+// Column-wise inclusive cumsum of the chunk's gate g (T x D) into shared memory
+// gcs[t * kGcPitch + d]; thread d owns channel d.  Also returns the channel's max, min and
+// whether a positive gate was seen.  (pipeline.py:21 / ref.py:14: gc = cumsum(g) per chunk.)
+constexpr int kGcPitch = 132;  // padded row pitch (floats): conflict-free row reads by row owners
+
+template <class TIn>
+__device__ __forceinline__ void chunk_cumsum(const TIn* __restrict__ g, float* gcs, float& mx, float& mn,
+                                             bool& pos) {
+  const int d = threadIdx.x;
+  float acc = 0.f;
+  mx = -3.0e38f;
+  mn = 3.0e38f;
+  pos = false;
+#pragma unroll 8
+  for (int t = 0; t < kT; ++t) {
+    const float x = to_f(g[t * kD + d]);
+    pos |= x > 0.f;
+    acc += x;
+    gcs[t * kGcPitch + d] = acc;
+    mx = fmaxf(mx, acc);
+    mn = fminf(mn, acc);
+  }
+}
+
+constexpr int kDV = 32;  // state columns per scan CTA
+
+struct ScanParams {
+  const uint8_t* img;      // per-chunk transition images, chunk-head stride img_stride bytes
+  uint32_t img_stride;
+  const float* add;        // per-chunk 128x128 additive term (Bc or Cc)
+  const float* state_in;   // (BH, D, D) initial state, or nullptr for zeros
+  float* states;           // per-chunk stored states: states[(bh * states_per_head + c) * D * D]
+  int states_per_head;     // NC + 1 (forward) or NC (backward)
+  int store_final_state;   // also store the final state at slot NC (forward)
+  float* final_out;        // (BH, D, D)
+  int NC;
+  int mode;                // gdn2_precision of the products
+  int reverse;
+  float clip;
+  unsigned* status;
+};
+
+cudaError_t launch_fwd_intra(const OpParams& p, bool bf16, int nblocks, cudaStream_t st);
+cudaError_t launch_fwd_out(const OpParams& p, bool bf16, float* o, int nblocks, cudaStream_t st);
+cudaError_t launch_scan(const ScanParams& sp, int BH, cudaStream_t st);
+
+}  // namespace gdn2

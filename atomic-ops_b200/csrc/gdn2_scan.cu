@@ -1,0 +1,147 @@
+// Sequential inter-chunk state scans (sm_100a), one CTA per (b, h, 32-column tile of d_v).
+//
+// Forward:   h_{c+1} = M_c h_c + Bc_c             (h_pre of every chunk and h_final stored)
+// Backward:  dh_c    = M_c^T dh_{c+1} + Cc_c       (dh entering every chunk from the right stored)
+//
+// Both are the same loop: the 128x128 transition operand of chunk c is a pre-encoded image
+// (hi/lo parts in the tensor core's K-major layout, written by fwd_intra) that one thread copies
+// into shared memory with a single bulk async copy while the previous chunk finishes; the state
+// tile (128 x 32, fp32 in registers: thread d owns row d) is the MMA's B operand.  Column tiles
+// of the state are independent because the transition acts on the d_k side only
+// (fwd/cd_slim.py:23-31, bwd/mega.py:31-34).
+#include "gdn2_kernels.cuh"
+
+namespace gdn2 {
+
+constexpr uint32_t kScanImg = 2 * 65536;                 // largest image (tf32, 3 passes)
+constexpr uint32_t kScanB = 2 * 16384;                   // state tile hi + lo
+constexpr uint32_t kScanSmem = 1024 + kScanImg + kScanB + 64;
+
+
+
+__global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanParams sp) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* img_s = sm;
+  uint8_t* b_s = sm + kScanImg;
+  uint64_t* bar_ld = reinterpret_cast<uint64_t*>(sm + kScanImg + kScanB);
+  uint64_t* bar_mma = bar_ld + 1;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_ld + 2);
+
+  const int t = threadIdx.x, warp = t >> 5;
+  const int tiles = kD / kDV;
+  const int bh = blockIdx.x / tiles, v0 = (blockIdx.x % tiles) * kDV;
+  const Mode m = mode_from_enum(sp.mode);
+  const uint32_t part = image_part_bytes(m);
+  const uint32_t ibytes = image_bytes(m);
+  const bool lo = m.passes == 3;
+  const size_t mat = (size_t)kD * kD;
+
+  if (warp == 0) {
+    tmem_alloc(tslot, 32);
+    tmem_relinquish();
+  }
+  if (t == 0) {
+    mbar_init(bar_ld, 1);
+    mbar_init(bar_mma, 1);
+    fence_mbar_init();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tb = *tslot;
+
+  auto chunk_of = [&](int it) { return sp.reverse ? sp.NC - 1 - it : it; };
+  auto issue_load = [&](int c) {
+    const uint8_t* src = sp.img + ((size_t)bh * sp.NC + c) * sp.img_stride;
+    mbar_arrive_expect_tx(bar_ld, ibytes);
+    for (uint32_t o = 0; o < ibytes; o += 32768u) bulk_g2s(img_s + o, src + o, 32768u, bar_ld);
+  };
+  if (t == 0) issue_load(chunk_of(0));
+
+  // State row t, columns v0 .. v0+31.
+  float h[kDV];
+  if (sp.state_in) {
+    const float* src = sp.state_in + (size_t)bh * mat + (size_t)t * kD + v0;
+#pragma unroll
+    for (int j = 0; j < kDV; j += 4) {
+      float4 x = *reinterpret_cast<const float4*>(src + j);
+      h[j] = x.x; h[j + 1] = x.y; h[j + 2] = x.z; h[j + 3] = x.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < kDV; ++j) h[j] = 0.f;
+  }
+
+  const Tile A[2] = {tile_k(smem_u32(img_s), 128u * (uint32_t)esize(m)),
+                     tile_k(smem_u32(img_s) + part, 128u * (uint32_t)esize(m))};
+  const uint32_t bpart = (m.fmt == kTF32) ? 16384u : 8192u;
+  const Tile Bt[2] = {tile_mn(smem_u32(b_s), kDV * (uint32_t)esize(m), m.fmt),
+                      tile_mn(smem_u32(b_s) + bpart, kDV * (uint32_t)esize(m), m.fmt)};
+  const int nsteps = 128 * esize(m) / 32;
+  uint32_t ph_ld = 0, ph_mma = 0;
+
+  for (int it = 0; it < sp.NC; ++it) {
+    const int c = chunk_of(it);
+    // store the state entering this chunk
+    {
+      float* dst = sp.states + ((size_t)bh * sp.states_per_head + c) * mat + (size_t)t * kD + v0;
+#pragma unroll
+      for (int j = 0; j < kDV; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(h[j], h[j + 1], h[j + 2], h[j + 3]);
+    }
+    // stage the state as the B operand (row t of the state = k index t)
+#pragma unroll
+    for (int j = 0; j < kDV; j += 8) stage_mnrow(Bt[0], Bt[1], lo, m.fmt, t, j, h + j, 8);
+    // prefetch the additive term
+    float add[kDV];
+    {
+      const float* src = sp.add + ((size_t)bh * sp.NC + c) * mat + (size_t)t * kD + v0;
+#pragma unroll
+      for (int j = 0; j < kDV; j += 4) {
+        float4 x = __ldg(reinterpret_cast<const float4*>(src + j));
+        add[j] = x.x; add[j + 1] = x.y; add[j + 2] = x.z; add[j + 3] = x.w;
+      }
+    }
+    staged_sync();
+    mbar_wait(bar_ld, ph_ld, sp.status);
+    ph_ld ^= 1u;
+    if (t == 0) {
+      tc_fence_after();
+      mma_tiles(m.fmt, m.passes, tb, A, Bt, kDV, nsteps, false, false);
+      mma_commit(bar_mma);
+    }
+    mbar_wait(bar_mma, ph_mma, sp.status);
+    ph_mma ^= 1u;
+    tc_fence_after();
+    if (t == 0 && it + 1 < sp.NC) issue_load(chunk_of(it + 1));
+    float acc[32];
+    tmem_ld32(tb, 0, acc);
+#pragma unroll
+    for (int j = 0; j < kDV; ++j) h[j] = sanitize(acc[j] + add[j], sp.clip);
+    tc_fence_before();
+    __syncthreads();  // all TMEM reads and B-tile reads done before the next iteration rewrites them
+    tc_fence_after();
+  }
+  {
+    float* dst = sp.final_out + (size_t)bh * mat + (size_t)t * kD + v0;
+#pragma unroll
+    for (int j = 0; j < kDV; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(h[j], h[j + 1], h[j + 2], h[j + 3]);
+    if (sp.store_final_state) {
+      float* d2 = sp.states + ((size_t)bh * sp.states_per_head + sp.NC) * mat + (size_t)t * kD + v0;
+#pragma unroll
+      for (int j = 0; j < kDV; j += 4) *reinterpret_cast<float4*>(d2 + j) = make_float4(h[j], h[j + 1], h[j + 2], h[j + 3]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tb, 32);
+}
+
+cudaError_t launch_scan(const ScanParams& sp, int BH, cudaStream_t st) {
+  cudaError_t e = cudaFuncSetAttribute(scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kScanSmem);
+  if (e != cudaSuccess) return e;
+  scan_kernel<<<BH * (kD / kDV), kThreads, kScanSmem, st>>>(sp);
+  return cudaGetLastError();
+}
+
+}  // namespace gdn2
