@@ -113,8 +113,40 @@ extern "C" gdn2_status gdn2_bwd(const gdn2_desc* d, const void* q, const void* k
                                 float* dh0, void* workspace, uint32_t* dev_status, void* stream) {
   gdn2_status s = check_desc(d);
   if (s != GDN2_OK) return s;
-  (void)q; (void)k; (void)v; (void)w; (void)b; (void)g; (void)residual; (void)d_o; (void)d_hfinal;
-  (void)dq; (void)dk; (void)dv; (void)dw; (void)db; (void)dg; (void)dh0; (void)workspace; (void)dev_status;
-  (void)stream;
-  return GDN2_ERR_UNSUPPORTED;
+  const void* ptrs[] = {q, k, v, w, b, g, d_o, dq, dk, dv, dw, db, dg, dh0};
+  for (const void* x : ptrs)
+    if (!x || !aligned16(x)) return GDN2_ERR_INVALID_ARGUMENT;
+  if ((d_hfinal && !aligned16(d_hfinal)) || !residual || !aligned256(residual) || !workspace ||
+      !aligned256(workspace) || !dev_status)
+    return GDN2_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool bf16 = d->in_dtype == GDN2_BF16;
+  BwdParams bp{};
+  bp.op = make_params(d, q, k, v, w, b, g, const_cast<void*>(residual), dev_status);
+  bp.d_o = d_o;
+  bp.dq = dq; bp.dk = dk; bp.dv = dv; bp.dw = dw; bp.db = db; bp.dg = dg;
+  bp.ws = static_cast<uint8_t*>(workspace);
+  const int BH = d->B * d->H, NC = bp.op.NC;
+  bp.wl = ws_layout(BH, NC);
+
+  if (launch_bwd_pre(bp, bf16, BH * NC, st) != cudaSuccess) return GDN2_ERR_CUDA;
+
+  ScanParams sp{};
+  sp.img = bp.op.res + bp.op.rl.mb;
+  sp.img_stride = bp.op.rl.mb_stride;
+  sp.add = reinterpret_cast<const float*>(bp.ws + bp.wl.cc);
+  sp.state_in = d_hfinal;
+  sp.states = reinterpret_cast<float*>(bp.ws + bp.wl.dhs);
+  sp.states_per_head = NC;
+  sp.store_final_state = 0;
+  sp.final_out = dh0;
+  sp.NC = NC;
+  sp.mode = d->b3_dot_mode;
+  sp.reverse = 1;
+  sp.clip = d->clip;
+  sp.status = dev_status;
+  if (launch_scan(sp, BH, st) != cudaSuccess) return GDN2_ERR_CUDA;
+
+  if (launch_bwd_intra(bp, bf16, BH * NC, st) != cudaSuccess) return GDN2_ERR_CUDA;
+  return GDN2_OK;
 }

@@ -1,0 +1,426 @@
+// Chunk-parallel backward kernels of the GDN-2 operator (sm_100a).
+//
+// Reference: atomic_gdn2/bwd/mega.py:9-58 (B1 .. B5 per chunk, reverse loop) and bwd/b4.py
+// (intra-chunk score backward).  The reverse dh recurrence of mega.py:31-34,
+//     dh_c = qg^T (scale do) + dh_{c+1} e^gl - wp^T (Aqk^T do + kg dh_{c+1}),
+// is rewritten as dh_c = M^T dh_{c+1} + Cc with the forward's transition M = diag(e^gl) - kg^T wp
+// and the chunk-local Cc = scale qg^T do - wp^T (Aqk^T do), so that
+//   bwd_pre    (chunk-parallel)  dvl = Aqk^T do and Cc,
+//   scan       (gdn2_scan.cu)    the sequential dh recurrence, storing dh entering every chunk,
+//   bwd_intra  (chunk-parallel)  everything else: dv_new, B3 (WY / inverse gradients), B4 and B5.
+//
+// bwd_intra folds the gate factors into the operands so that the six gradients accumulate in
+// four tensor-memory accumulators.  With m the chunk's per-channel reference point,
+// E = e^(gc - m), F = e^(m - gc):
+//   Dq  = E o [ do (scale e^m h_pre)^T          + scale dAqk (k F) ]            = dq
+//   Dbk = E o [ A^T dwp'                        + dAkk (k F) ]                  = dL/d(b k)
+//         with dwp' = -dv_new (e^m h_pre)^T  (so that A^T dwp' = dkb e^m)
+//   Dk  = F o [ (E o Dbk o b) + v_new (e^(gl-m) dh_next)^T + scale dAqk^T (q E) + dAkk^T (b k E) ]
+// and dgc = q o Dq + 2 (b k) o Dbk - k o Dk, plus, on the chunk's last row,
+// sum_v dh_next[d, v] h_next[d, v] (the derivative through the chunk decay e^gl; it equals the
+// reference's dgc_last + the last-row kg term, mega.py:43-49).  dg is the reverse cumsum of dgc
+// (mega.py:51, B5).
+#include "gdn2_kernels.cuh"
+
+namespace gdn2 {
+
+constexpr uint32_t kPreSmem = 1024 + 6 * 16384 + kT * kGcPitch * 4 + 64;
+constexpr uint32_t kBwdSmem = 1024 + 8 * 16384 + kT * kGcPitch * 4 + 3 * kD * 4 + 64;
+
+__device__ __forceinline__ uint8_t* align1024b(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+// ---------------------------------------------------------------------------------------
+// bwd_pre: dvl = Aqk^T do,  Cc = scale qg^T do - wp^T dvl      (b3_dot_mode, mega.py:31-34)
+// ---------------------------------------------------------------------------------------
+template <class TIn>
+__global__ void __launch_bounds__(kThreads, 1) bwd_pre_kernel(const BwdParams P) {
+  extern __shared__ uint8_t smem_raw[];
+  const OpParams& p = P.op;
+  uint8_t* sm = align1024b(smem_raw);
+  const uint32_t pool = smem_u32(sm);
+  float* gcs = reinterpret_cast<float*>(sm + 6 * 16384);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + 6 * 16384 + kT * kGcPitch * 4);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 1);
+
+  const int t = threadIdx.x, warp = t >> 5;
+  const int ch = blockIdx.x, bh = ch / p.NC, c = ch % p.NC;
+  const long long off = chunk_off(p, bh, c);
+  const TIn* q = reinterpret_cast<const TIn*>(p.q) + off;
+  const TIn* g = reinterpret_cast<const TIn*>(p.g) + off;
+  const float* do_ = P.d_o + off;
+  const size_t mat = (size_t)kT * kD;
+  const float* aqk_g = reinterpret_cast<const float*>(p.res + p.rl.aqk) + (size_t)ch * mat;
+  const float* wp_g = reinterpret_cast<const float*>(p.res + p.rl.wp) + (size_t)ch * mat;
+  float* dvl_g = reinterpret_cast<float*>(P.ws + P.wl.dvl) + (size_t)ch * mat;
+  float* cc_g = reinterpret_cast<float*>(P.ws + P.wl.cc) + (size_t)ch * mat;
+  const Mode m3 = mode_from_enum(p.b3_mode);
+  const float clip = p.clip, scale = p.scale;
+
+  if (warp == 0) {
+    tmem_alloc(tslot, 256);
+    tmem_relinquish();
+  }
+  if (t == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  {
+    float mx, mn;
+    bool pos;
+    chunk_cumsum(g, gcs, mx, mn, pos);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tb = *tslot;
+  const uint32_t S0 = tb, S1 = tb + 128;
+  MmaBar mb{bar, 0u, p.status};
+
+  auto src_aqk = [&](int r, int c0, float* x) { ld32_f(aqk_g + r * kT + c0, x); };
+  auto src_do = [&](int r, int c0, float* x) { ld32_f(do_ + r * kD + c0, x); };
+  auto src_qg = [&](int r, int c0, float* x) {
+    ld32_in(q + r * kD + c0, x);
+    const float* gr = gcs + r * kGcPitch + c0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) x[j] = scale * sanitize(x[j] * ex(fminf(gr[j], 0.f)), clip);
+  };
+  auto src_wp = [&](int r, int c0, float* x) { ld32_f(wp_g + r * kD + c0, x); };
+  auto src_s0 = [&](int, int c0, float* x) { tmem_ld32(S0, (uint32_t)c0, x); };
+
+  // S0 = Aqk^T do, S1 = (scale qg)^T do   (shared B = do)
+  gemm_pairs(m3, pool, mb, S0, true, src_aqk, true, src_do, false, false, 2, S1, true, src_qg, true, src_do, false,
+             false, false, true);
+  for (int c0 = 0; c0 < kD; c0 += 32) {
+    float x[32];
+    tmem_ld32(S0, c0, x);
+    st32_f(dvl_g + t * kD + c0, x);
+  }
+  // S1 -= wp^T dvl
+  gemm_pairs(m3, pool, mb, S1, true, src_wp, true, src_s0, true, true);
+  for (int c0 = 0; c0 < kD; c0 += 32) {
+    float x[32];
+    tmem_ld32(S1, c0, x);
+    st32_f(cc_g + t * kD + c0, x);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tb, 256);
+}
+
+// ---------------------------------------------------------------------------------------
+// bwd_intra
+// ---------------------------------------------------------------------------------------
+template <class TIn>
+__global__ void __launch_bounds__(kThreads, 1) bwd_intra_kernel(const BwdParams P) {
+  extern __shared__ uint8_t smem_raw[];
+  const OpParams& p = P.op;
+  uint8_t* sm = align1024b(smem_raw);
+  const uint32_t pool = smem_u32(sm);
+  float* gcs = reinterpret_cast<float*>(sm + 8 * 16384);
+  float* mid_s = gcs + kT * kGcPitch;
+  float* gl_s = mid_s + kD;
+  float* extra_s = gl_s + kD;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(extra_s + kD);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 1);
+
+  const int t = threadIdx.x, warp = t >> 5;
+  const int ch = blockIdx.x, bh = ch / p.NC, c = ch % p.NC;
+  const long long off = chunk_off(p, bh, c);
+  const TIn* q = reinterpret_cast<const TIn*>(p.q) + off;
+  const TIn* k = reinterpret_cast<const TIn*>(p.k) + off;
+  const TIn* v = reinterpret_cast<const TIn*>(p.v) + off;
+  const TIn* w = reinterpret_cast<const TIn*>(p.w) + off;
+  const TIn* b = reinterpret_cast<const TIn*>(p.b) + off;
+  const TIn* g = reinterpret_cast<const TIn*>(p.g) + off;
+  const float* do_ = P.d_o + off;
+  TIn* dq = reinterpret_cast<TIn*>(P.dq) + off;
+  TIn* dk = reinterpret_cast<TIn*>(P.dk) + off;
+  TIn* dv = reinterpret_cast<TIn*>(P.dv) + off;
+  TIn* dw = reinterpret_cast<TIn*>(P.dw) + off;
+  TIn* db = reinterpret_cast<TIn*>(P.db) + off;
+  TIn* dg = reinterpret_cast<TIn*>(P.dg) + off;
+  const size_t mat = (size_t)kT * kD;
+  const float* ainv_g = reinterpret_cast<const float*>(p.res + p.rl.ainv) + (size_t)ch * mat;
+  const float* hpre_g = reinterpret_cast<const float*>(p.res + p.rl.hs) + ((size_t)bh * (p.NC + 1) + c) * mat;
+  const float* hnext_g = hpre_g + mat;
+  const float* vnew_g = reinterpret_cast<const float*>(p.res + p.rl.vnew) + (size_t)ch * mat;
+  const float* dvl_g = reinterpret_cast<const float*>(P.ws + P.wl.dvl) + (size_t)ch * mat;
+  const float* dhn_g = reinterpret_cast<const float*>(P.ws + P.wl.dhs) + (size_t)ch * mat;
+  const Mode m3 = mode_from_enum(p.b3_mode);
+  const Mode mh = mode_from_enum(GDN2_PREC_HIGHEST);  // B4 products are fixed at "highest" (mega.py:13)
+  const float clip = p.clip, scale = p.scale;
+
+  if (warp == 0) {
+    tmem_alloc(tslot, 512);
+    tmem_relinquish();
+  }
+  if (t == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  {
+    float mx, mn;
+    bool pos;
+    chunk_cumsum(g, gcs, mx, mn, pos);
+    mid_s[t] = 0.5f * (mx + mn);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  gl_s[t] = gcs[(kT - 1) * kGcPitch + t];
+  {
+    // last-row decay term: sum_v dh_next[d, v] h_next[d, v] for channel d = t
+    float acc = 0.f;
+    for (int c0 = 0; c0 < kD; c0 += 32) {
+      float a[32], h[32];
+      ld32_f(dhn_g + t * kD + c0, a);
+      ld32_f(hnext_g + t * kD + c0, h);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) acc = fmaf(a[j], h[j], acc);
+    }
+    extra_s[t] = acc;
+  }
+  __syncthreads();
+  const uint32_t tb = *tslot;
+  const uint32_t S0 = tb, S1 = tb + 128, S2 = tb + 256, S3 = tb + 384;
+  MmaBar mb{bar, 0u, p.status};
+
+  // ---- row sources (row r is always the calling thread's own row) ----
+  auto gcrow = [&](int r) { return gcs + r * kGcPitch; };
+  auto src_kg = [&](int r, int c0, float* x) {
+    ld32_in(k + r * kD + c0, x);
+    const float* gr = gcrow(r) + c0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) x[j] = sanitize(x[j] * ex(fminf(gl_s[c0 + j] - gr[j], 0.f)), clip);
+  };
+  auto src_dhn = [&](int r, int c0, float* x) { ld32_f(dhn_g + r * kD + c0, x); };
+  auto src_hpre_em = [&](int r, int c0, float* x) {  // row d = r of e^m h_pre
+    ld32_f(hpre_g + r * kD + c0, x);
+    const float s = ex(mid_s[r]);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) x[j] *= s;
+  };
+  auto src_dhn_gl = [&](int r, int c0, float* x) {  // row d = r of e^(gl-m) dh_next
+    ld32_f(dhn_g + r * kD + c0, x);
+    const float s = ex(gl_s[r] - mid_s[r]);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) x[j] *= s;
+  };
+  auto src_bkE = [&](int r, int c0, float* x) {
+    float kv[32];
+    ld32_in(b + r * kD + c0, x);
+    ld32_in(k + r * kD + c0, kv);
+    const float* gr = gcrow(r) + c0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) x[j] = x[j] * kv[j] * ex(gr[j] - mid_s[c0 + j]);
+  };
+  auto src_qE = [&](int r, int c0, float* x) {
+    ld32_in(q + r * kD + c0, x);
+    const float* gr = gcrow(r) + c0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) x[j] = scale * x[j] * ex(gr[j] - mid_s[c0 + j]);
+  };
+  auto src_kF = [&](int r, int c0, float* x) {
+    ld32_in(k + r * kD + c0, x);
+    const float* gr = gcrow(r) + c0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) x[j] = x[j] * ex(mid_s[c0 + j] - gr[j]);
+  };
+  auto src_wv = [&](int r, int c0, float* x) {
+    float vv[32];
+    ld32_in(w + r * kD + c0, x);
+    ld32_in(v + r * kD + c0, vv);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) x[j] *= vv[j];
+  };
+  auto src_ainv = [&](int r, int c0, float* x) { ld32_f(ainv_g + r * kT + c0, x); };
+  auto src_vnew = [&](int r, int c0, float* x) { ld32_f(vnew_g + r * kD + c0, x); };
+  auto src_do = [&](int r, int c0, float* x) { ld32_f(do_ + r * kD + c0, x); };
+  auto src_do_s = [&](int r, int c0, float* x) {
+    ld32_f(do_ + r * kD + c0, x);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) x[j] *= scale;
+  };
+  auto tm = [&](uint32_t slot) { return [=](int, int c0, float* x) { tmem_ld32(slot, (uint32_t)c0, x); }; };
+  auto tm_scaled = [&](uint32_t slot) {
+    return [=](int, int c0, float* x) {
+      tmem_ld32(slot, (uint32_t)c0, x);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) x[j] *= scale;
+    };
+  };
+
+  // 1. S0 = dv_new = sanitize(dvl + kg dh_next)                                  [B1, b3 mode]
+  gemm_pairs(m3, pool, mb, S0, false, src_kg, true, src_dhn, false, false);
+  for (int c0 = 0; c0 < kD; c0 += 32) {
+    float x[32], y[32];
+    tmem_ld32(S0, c0, x);
+    ld32_f(dvl_g + t * kD + c0, y);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) x[j] = sanitize(x[j] + y[j], clip);
+    tmem_st32(S0, c0, x);
+  }
+  // 2. S1 = dwp' = -dv_new (e^m h_pre)^T                                          [B3]
+  gemm_pairs(m3, pool, mb, S1, false, tm(S0), false, src_hpre_em, true, false);
+  // 3. S2 = dA = sanitize(dwp' (bk E)^T + dv_new (w v)^T)                          [B3]
+  gemm_pairs(m3, pool, mb, S2, false, tm(S1), false, src_bkE, false, false, 2, S2, false, tm(S0), false, src_wv,
+             false, true);
+  for (int c0 = 0; c0 < kT; c0 += 32) {
+    float x[32];
+    tmem_ld32(S2, c0, x);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) x[j] = sanitize(x[j], clip);
+    tmem_st32(S2, c0, x);
+  }
+  // 4. S3 = dwv = A^T dv_new;  dw = dwv v, dv = dwv w                              [B3]
+  gemm_pairs(m3, pool, mb, S3, true, src_ainv, true, tm(S0), false, false);
+  for (int c0 = 0; c0 < kD; c0 += 32) {
+    float x[32], a[32], y[32];
+    tmem_ld32(S3, c0, x);
+    ld32_in(v + t * kD + c0, a);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) y[j] = sanitize(x[j] * a[j], clip);
+    st32_out(dw + t * kD + c0, y);
+    ld32_in(w + t * kD + c0, a);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) y[j] = sanitize(x[j] * a[j], clip);
+    st32_out(dv + t * kD + c0, y);
+  }
+  // 5. S0 = tmp = sanitize(dA A^T)                                                   [B3]
+  gemm_pairs(m3, pool, mb, S0, false, tm(S2), false, src_ainv, false, false);
+  for (int c0 = 0; c0 < kT; c0 += 32) {
+    float x[32];
+    tmem_ld32(S0, c0, x);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) x[j] = sanitize(x[j], clip);
+    tmem_st32(S0, c0, x);
+  }
+  // 6. S2 = dAkk = sanitize(-(1-eps) A^T tmp) strict                                  [B3]
+  gemm_pairs(m3, pool, mb, S2, true, src_ainv, true, tm(S0), true, false);
+  {
+    const float keep = 1.0f - p.eps;
+    for (int c0 = 0; c0 < kT; c0 += 32) {
+      float x[32];
+      tmem_ld32(S2, c0, x);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) x[j] = (c0 + j < t) ? sanitize(x[j] * keep, clip) : 0.f;
+      tmem_st32(S2, c0, x);
+    }
+  }
+  // 7. S0 = A^T dwp' (B3)  +  dAkk (k F) (B4, highest)
+  gemm_pairs(m3, pool, mb, S0, true, src_ainv, true, tm(S1), false, false);
+  gemm_pairs(mh, pool, mb, S0, false, tm(S2), true, src_kF, false, true);
+  // 8. S1 = dAqk = (do v_new^T) causal                                              [B2]
+  gemm_pairs(m3, pool, mb, S1, false, src_do, false, src_vnew, false, false);
+  for (int c0 = 0; c0 < kT; c0 += 32) {
+    float x[32];
+    tmem_ld32(S1, c0, x);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) x[j] = (c0 + j <= t) ? x[j] : 0.f;
+    tmem_st32(S1, c0, x);
+  }
+  // 9. S3 = scale do (e^m h_pre)^T (B3)  +  scale dAqk (k F) (B4)
+  gemm_pairs(m3, pool, mb, S3, false, src_do_s, false, src_hpre_em, false, false);
+  gemm_pairs(mh, pool, mb, S3, false, tm_scaled(S1), true, src_kF, false, true);
+  // 10.-11. finish dq and db;  S3 <- dgc partial;  S0 <- Dbk b E (pre-scaled dk partial)
+  {
+    const float* gr = gcrow(t);
+    for (int c0 = 0; c0 < kD; c0 += 32) {
+      float x[32], y[32], qv[32], kv[32], bv[32], E[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) E[j] = ex(gr[c0 + j] - mid_s[c0 + j]);
+      ld32_in(q + t * kD + c0, qv);
+      ld32_in(k + t * kD + c0, kv);
+      ld32_in(b + t * kD + c0, bv);
+      tmem_ld32(S3, c0, x);  // Dq / E
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        x[j] *= E[j];
+        y[j] = sanitize(x[j], clip);
+      }
+      st32_out(dq + t * kD + c0, y);
+      float dgcp[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) dgcp[j] = qv[j] * x[j];
+      tmem_ld32(S0, c0, x);  // Dbk / E
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        x[j] *= E[j];
+        y[j] = sanitize(x[j] * kv[j], clip);
+        dgcp[j] += 2.f * bv[j] * kv[j] * x[j];
+        x[j] = x[j] * bv[j] * E[j];
+      }
+      st32_out(db + t * kD + c0, y);
+      tmem_st32(S3, c0, dgcp);
+      tmem_st32(S0, c0, x);
+    }
+  }
+  // 12. S0 += v_new (e^(gl-m) dh_next)^T (B3)  +  scale dAqk^T (q E) + dAkk^T (bk E) (B4)
+  gemm_pairs(m3, pool, mb, S0, false, src_vnew, false, src_dhn_gl, false, true);
+  gemm_pairs(mh, pool, mb, S0, true, tm(S1), true, src_qE, false, true, 2, S0, true, tm(S2), true, src_bkE, false,
+             true);
+  // 13. dk = F o S0;  dgc = S3 - k o dk (+ decay term on the last row);  dgc -> smem (gcs rows)
+  {
+    float* gr = gcs + t * kGcPitch;
+    for (int c0 = 0; c0 < kD; c0 += 32) {
+      float x[32], y[32], kv[32], dgcp[32];
+      ld32_in(k + t * kD + c0, kv);
+      tmem_ld32(S0, c0, x);
+      tmem_ld32(S3, c0, dgcp);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        x[j] *= ex(mid_s[c0 + j] - gr[c0 + j]);
+        y[j] = sanitize(x[j], clip);
+        dgcp[j] -= kv[j] * x[j];
+        if (t == kT - 1) dgcp[j] += extra_s[c0 + j];
+      }
+      st32_out(dk + t * kD + c0, y);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) gr[c0 + j] = dgcp[j];
+    }
+  }
+  __syncthreads();
+  // 14. dg = reverse cumsum of dgc over the chunk (B5)
+  {
+    float acc = 0.f;
+    for (int r = kT - 1; r >= 0; --r) {
+      acc += gcs[r * kGcPitch + t];
+      const float val = sanitize(acc, clip);
+      if constexpr (sizeof(TIn) == 4) {
+        dg[r * kD + t] = val;
+      } else {
+        dg[r * kD + t] = __float2bfloat16_rn(val);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tb, 512);
+}
+
+template <class TIn>
+static cudaError_t launch_bwd_pre_t(const BwdParams& p, int nblocks, cudaStream_t st) {
+  cudaError_t e = cudaFuncSetAttribute(bwd_pre_kernel<TIn>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPreSmem);
+  if (e != cudaSuccess) return e;
+  bwd_pre_kernel<TIn><<<nblocks, kThreads, kPreSmem, st>>>(p);
+  return cudaGetLastError();
+}
+template <class TIn>
+static cudaError_t launch_bwd_intra_t(const BwdParams& p, int nblocks, cudaStream_t st) {
+  cudaError_t e =
+      cudaFuncSetAttribute(bwd_intra_kernel<TIn>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBwdSmem);
+  if (e != cudaSuccess) return e;
+  bwd_intra_kernel<TIn><<<nblocks, kThreads, kBwdSmem, st>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bwd_pre(const BwdParams& p, bool bf16, int nblocks, cudaStream_t st) {
+  return bf16 ? launch_bwd_pre_t<__nv_bfloat16>(p, nblocks, st) : launch_bwd_pre_t<float>(p, nblocks, st);
+}
+cudaError_t launch_bwd_intra(const BwdParams& p, bool bf16, int nblocks, cudaStream_t st) {
+  return bf16 ? launch_bwd_intra_t<__nv_bfloat16>(p, nblocks, st) : launch_bwd_intra_t<float>(p, nblocks, st);
+}
+
+}  // namespace gdn2

@@ -200,6 +200,97 @@ __device__ __forceinline__ void chunk_cumsum(const TIn* __restrict__ g, float* g
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Generic K-loop over one or two operand pairs (all M = N = 128, K = 128).
+// Operands come from "row sources": src(row, c0, out32) returns 32 consecutive values of row
+// `row` of the source matrix starting at column c0.  A K-major operand (mn = false) is the
+// source itself (row = M/N index, column = K index): every thread stages its own row.  An
+// MN-major operand (mn = true) is the transpose of the source (source row = K index): only the
+// warp(s) whose rows fall in the current K-slice stage.  TMEM-backed sources are warp-collective,
+// which both patterns respect (whole warps call them).
+// ---------------------------------------------------------------------------
+template <class Src>
+__device__ __forceinline__ void stage_operand(const Tile tt[2], bool mn, Mode m, int k0, int KS, Src src) {
+  const int t = threadIdx.x, warp = t >> 5;
+  const bool lo = m.passes == 3;
+  if (!mn) {
+    for (int i = 0; i < KS; i += 32) {
+      float x[32];
+      src(t, k0 + i, x);
+      stage_krow(tt[0], tt[1], lo, m.fmt, (uint32_t)t, i, x, 32);
+    }
+  } else if (warp * 32 >= k0 && warp * 32 < k0 + KS) {
+    for (int c0 = 0; c0 < 128; c0 += 32) {
+      float x[32];
+      src(t, c0, x);
+      stage_mnrow(tt[0], tt[1], lo, m.fmt, (uint32_t)(t - k0), c0, x, 32);
+    }
+  }
+}
+
+struct NoSrc {
+  __device__ void operator()(int, int, float*) const {}
+};
+
+// D1 (+)= op(A1) op(B1)  [and D2 (+)= op(A2) op(B2)], sharing the K-slicing of mode m.
+// share_a / share_b reuse pair 1's staged A / B for pair 2.
+template <class SA1, class SB1, class SA2 = NoSrc, class SB2 = NoSrc>
+__device__ __forceinline__ void gemm_pairs(Mode m, uint32_t pool, MmaBar& mb,
+                                           uint32_t d1, bool a1mn, SA1 sa1, bool b1mn, SB1 sb1, bool neg1,
+                                           bool acc1, int npairs = 1, uint32_t d2 = 0, bool a2mn = false,
+                                           SA2 sa2 = SA2(), bool b2mn = false, SB2 sb2 = SB2(), bool neg2 = false,
+                                           bool acc2 = false, bool share_a = false, bool share_b = false) {
+  const int KS = kslice(m), ns = 128 / KS;
+  auto tiles = [&](int i, bool mn, Tile out[2]) {
+    out[0] = mn ? pool_mn(pool, i, m) : pool_k(pool, i);
+    out[1] = mn ? pool_mn(pool, i + 1, m) : pool_k(pool, i + 1);
+  };
+  for (int s = 0; s < ns; ++s) {
+    const int k0 = s * KS;
+    Tile A1[2], B1[2], A2[2], B2[2];
+    int nt = 0;
+    tiles(nt, a1mn, A1); nt += 2;
+    tiles(nt, b1mn, B1); nt += 2;
+    stage_operand(A1, a1mn, m, k0, KS, sa1);
+    stage_operand(B1, b1mn, m, k0, KS, sb1);
+    if (npairs == 2) {
+      if (share_a) { A2[0] = A1[0]; A2[1] = A1[1]; } else { tiles(nt, a2mn, A2); nt += 2; stage_operand(A2, a2mn, m, k0, KS, sa2); }
+      if (share_b) { B2[0] = B1[0]; B2[1] = B1[1]; } else { tiles(nt, b2mn, B2); nt += 2; stage_operand(B2, b2mn, m, k0, KS, sb2); }
+    }
+    staged_sync();
+    if (threadIdx.x == 0) {
+      tc_fence_after();
+      issue_slice(m, d1, A1, B1, 128, neg1, acc1 || s > 0);
+      if (npairs == 2) issue_slice(m, d2, A2, B2, 128, neg2, acc2 || s > 0);
+    }
+    mb.commit_wait();
+  }
+}
+
+// Row sources
+template <class TIn>
+__device__ __forceinline__ void ld32_in(const TIn* p, float* x) {
+#pragma unroll
+  for (int j = 0; j < 32; j += 4) ld4(p + j, x + j);
+}
+__device__ __forceinline__ void ld32_f(const float* p, float* x) {
+#pragma unroll
+  for (int j = 0; j < 32; j += 4) {
+    float4 v = *reinterpret_cast<const float4*>(p + j);
+    x[j] = v.x; x[j + 1] = v.y; x[j + 2] = v.z; x[j + 3] = v.w;
+  }
+}
+__device__ __forceinline__ void st32_f(float* p, const float* x) {
+#pragma unroll
+  for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(p + j) = make_float4(x[j], x[j + 1], x[j + 2], x[j + 3]);
+}
+__device__ __forceinline__ void st32_out(float* p, const float* x) { st32_f(p, x); }
+__device__ __forceinline__ void st32_out(__nv_bfloat16* p, const float* x) {
+#pragma unroll
+  for (int j = 0; j < 32; j += 4) st4(p + j, x + j);
+}
+
 constexpr int kDV = 32;  // state columns per scan CTA
 
 struct ScanParams {
@@ -221,5 +312,15 @@ struct ScanParams {
 cudaError_t launch_fwd_intra(const OpParams& p, bool bf16, int nblocks, cudaStream_t st);
 cudaError_t launch_fwd_out(const OpParams& p, bool bf16, float* o, int nblocks, cudaStream_t st);
 cudaError_t launch_scan(const ScanParams& sp, int BH, cudaStream_t st);
+
+struct BwdParams {
+  OpParams op;
+  const float* d_o;        // (B,H,L,D) fp32 cotangent of o (same strides as the inputs)
+  void* dq; void* dk; void* dv; void* dw; void* db; void* dg;  // (B,H,L,D) in the input dtype
+  uint8_t* ws;             // backward workspace
+  WsLayout wl;
+};
+cudaError_t launch_bwd_pre(const BwdParams& p, bool bf16, int nblocks, cudaStream_t st);
+cudaError_t launch_bwd_intra(const BwdParams& p, bool bf16, int nblocks, cudaStream_t st);
 
 }  // namespace gdn2
