@@ -36,7 +36,9 @@ class Gdn2Desc(ctypes.Structure):
 
 
 EXPORTS = ("gdn2_residual_bytes", "gdn2_bwd_workspace_bytes", "gdn2_fwd", "gdn2_bwd",
-           "gdn2_status_string", "gdn2_selftest_gemm")
+           "gdn2_status_string", "gdn2_selftest_gemm", "gdn2_profile_enable", "gdn2_profile_collect")
+# kernel ids of gdn2_profile_collect
+KERNELS = ("fwd_intra", "fwd_scan", "fwd_out", "bwd_pre", "bwd_scan", "bwd_intra")
 
 
 def _declare(lib):
@@ -53,7 +55,24 @@ def _declare(lib):
     lib.gdn2_status_string.argtypes = [ctypes.c_int]
     lib.gdn2_selftest_gemm.restype = ctypes.c_int
     lib.gdn2_selftest_gemm.argtypes = [P, P, P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, P, P]
+    lib.gdn2_profile_enable.restype = None
+    lib.gdn2_profile_enable.argtypes = [ctypes.c_int32]
+    lib.gdn2_profile_collect.restype = ctypes.c_int32
+    lib.gdn2_profile_collect.argtypes = [P, P, ctypes.c_int32]
     return lib
+
+
+def profile_enable(on: bool) -> None:
+    load().gdn2_profile_enable(1 if on else 0)
+
+
+def profile_collect() -> dict:
+    """{kernel: (summed ms, launches)} of the launches timed since the last collect (synchronises)."""
+    n = len(KERNELS)
+    ms = (ctypes.c_float * n)()
+    cnt = (ctypes.c_int32 * n)()
+    load().gdn2_profile_collect(ctypes.cast(ms, ctypes.c_void_p), ctypes.cast(cnt, ctypes.c_void_p), n)
+    return {k: (float(ms[i]), int(cnt[i])) for i, k in enumerate(KERNELS)}
 
 
 def lib_path() -> pathlib.Path:

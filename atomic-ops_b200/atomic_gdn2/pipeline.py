@@ -104,14 +104,22 @@ class _GDN2(torch.autograd.Function):
         dev = q.device
         nc = L // cfg.bt
         seg = cfg.max_chunks_per_call
-        o = torch.empty((B, H, L, D), dtype=torch.float32, device=dev)
+        # o shares the inputs' (b, h) strides: the C ABI addresses every (B,H,L,D) tensor of a call
+        # with one stride pair (views of longer sequences are consumed without copies)
+        o = torch.empty_strided((B, H, L, D), q.stride(), dtype=torch.float32, device=dev)
         status = torch.zeros(1, dtype=torch.int32, device=dev)
+        # strides of size-1 dims are never used to form an address; give them canonical values
+        sb, sh = q.stride(0), q.stride(1)
+        if H == 1:
+            sh = max(sh, L * D)
+        if B == 1:
+            sb = max(sb, H * sh)
         h = h0
         segments, residuals = [], []
         for s in range(0, nc, seg):
             e = min(nc, s + seg)
             a = s * cfg.bt
-            desc = _make_desc(cfg, scale, B, H, (e - s) * cfg.bt, D, q.stride(0), q.stride(1), q.dtype)
+            desc = _make_desc(cfg, scale, B, H, (e - s) * cfg.bt, D, sb, sh, q.dtype)
             nbytes = lib.gdn2_residual_bytes(ctypes.byref(desc))
             if nbytes == 0:
                 _lib.check(_lib.ERR_INVALID_ARGUMENT, "gdn2_residual_bytes")
@@ -145,14 +153,15 @@ class _GDN2(torch.autograd.Function):
         dev = q.device
         if any(r is None for r in ctx.residuals):
             raise RuntimeError("gdn2: backward through a call made without gradient tracking")
-        do = (torch.zeros((B, H, L, D), dtype=torch.float32, device=dev) if do is None
-              else do.to(torch.float32))
-        if do.stride(-1) != 1 or do.stride(-2) != D or do.stride(0) != q.stride(0) or do.stride(1) != q.stride(1):
-            do = do.contiguous()
-            if do.stride(0) != q.stride(0) or do.stride(1) != q.stride(1):
-                raise RuntimeError("gdn2: cotangent layout does not match the inputs")
+        # every (B,H,L,D) tensor of a call shares the inputs' strides (see forward)
+        do_s = torch.empty_strided((B, H, L, D), q.stride(), dtype=torch.float32, device=dev)
+        if do is None:
+            do_s.zero_()
+        else:
+            do_s.copy_(do)
+        do = do_s
         dh = None if dhf is None else dhf.to(torch.float32).contiguous()
-        grads = [torch.empty_like(t) for t in (q, k, v, w, b, g)]
+        grads = [torch.empty_strided(t.shape, q.stride(), dtype=t.dtype, device=dev) for t in (q, k, v, w, b, g)]
         status = torch.zeros(1, dtype=torch.int32, device=dev)
         el = q.element_size()
         for sgm, res in zip(reversed(ctx.segments), reversed(ctx.residuals)):

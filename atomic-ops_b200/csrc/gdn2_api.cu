@@ -1,4 +1,7 @@
 // C-ABI entry points: argument validation, residual / workspace layout and kernel orchestration.
+#include <mutex>
+#include <vector>
+
 #include "gdn2_kernels.cuh"
 
 using namespace gdn2;
@@ -59,7 +62,64 @@ OpParams make_params(const gdn2_desc* d, const void* q, const void* k, const voi
   return p;
 }
 
+// Optional per-kernel timing: CUDA events recorded on the launching stream around every kernel
+// launch while enabled (gdn2_profile_enable), summed per kernel by gdn2_profile_collect.
+struct KernelTimer {
+  std::mutex mu;
+  bool on = false;
+  struct Rec { int id; cudaEvent_t a, b; };
+  std::vector<Rec> recs;
+  std::vector<cudaEvent_t> spare;
+  cudaEvent_t get() {
+    if (!spare.empty()) { cudaEvent_t e = spare.back(); spare.pop_back(); return e; }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+  }
+};
+KernelTimer& ktimer() { static KernelTimer t; return t; }
+
+// Launch `f` (returns cudaError_t) bracketed by timing events when profiling is on.
+template <class F>
+cudaError_t timed(int id, cudaStream_t st, F f) {
+  KernelTimer& kt = ktimer();
+  if (!kt.on) return f();
+  std::lock_guard<std::mutex> g(kt.mu);
+  cudaEvent_t a = kt.get(), b = kt.get();
+  cudaEventRecord(a, st);
+  cudaError_t e = f();
+  cudaEventRecord(b, st);
+  kt.recs.push_back({id, a, b});
+  return e;
+}
+
 }  // namespace
+
+extern "C" void gdn2_profile_enable(int32_t enable) {
+  KernelTimer& kt = ktimer();
+  std::lock_guard<std::mutex> g(kt.mu);
+  kt.on = enable != 0;
+}
+
+extern "C" int32_t gdn2_profile_collect(float* ms, int32_t* counts, int32_t n) {
+  KernelTimer& kt = ktimer();
+  std::lock_guard<std::mutex> g(kt.mu);
+  for (int i = 0; i < n; ++i) { ms[i] = 0.f; counts[i] = 0; }
+  int32_t total = 0;
+  for (auto& r : kt.recs) {
+    float t = 0.f;
+    if (cudaEventSynchronize(r.b) == cudaSuccess && cudaEventElapsedTime(&t, r.a, r.b) == cudaSuccess &&
+        r.id >= 0 && r.id < n) {
+      ms[r.id] += t;
+      counts[r.id] += 1;
+      ++total;
+    }
+    kt.spare.push_back(r.a);
+    kt.spare.push_back(r.b);
+  }
+  kt.recs.clear();
+  return total;
+}
 
 extern "C" size_t gdn2_residual_bytes(const gdn2_desc* d) {
   if (check_desc(d) != GDN2_OK) return 0;
@@ -85,7 +145,8 @@ extern "C" gdn2_status gdn2_fwd(const gdn2_desc* d, const void* q, const void* k
   const OpParams p = make_params(d, q, k, v, w, b, g, residual, dev_status);
   const int BH = d->B * d->H, NC = p.NC;
 
-  if (launch_fwd_intra(p, bf16, BH * NC, st) != cudaSuccess) return GDN2_ERR_CUDA;
+  if (timed(GDN2_K_FWD_INTRA, st, [&] { return launch_fwd_intra(p, bf16, BH * NC, st); }) != cudaSuccess)
+    return GDN2_ERR_CUDA;
 
   ScanParams sp{};
   sp.img = p.res + p.rl.mf;
@@ -101,9 +162,10 @@ extern "C" gdn2_status gdn2_fwd(const gdn2_desc* d, const void* q, const void* k
   sp.reverse = 0;
   sp.clip = d->clip;
   sp.status = dev_status;
-  if (launch_scan(sp, BH, st) != cudaSuccess) return GDN2_ERR_CUDA;
+  if (timed(GDN2_K_FWD_SCAN, st, [&] { return launch_scan(sp, BH, st); }) != cudaSuccess) return GDN2_ERR_CUDA;
 
-  if (launch_fwd_out(p, bf16, o, BH * NC, st) != cudaSuccess) return GDN2_ERR_CUDA;
+  if (timed(GDN2_K_FWD_OUT, st, [&] { return launch_fwd_out(p, bf16, o, BH * NC, st); }) != cudaSuccess)
+    return GDN2_ERR_CUDA;
   return GDN2_OK;
 }
 
@@ -129,7 +191,8 @@ extern "C" gdn2_status gdn2_bwd(const gdn2_desc* d, const void* q, const void* k
   const int BH = d->B * d->H, NC = bp.op.NC;
   bp.wl = ws_layout(BH, NC);
 
-  if (launch_bwd_pre(bp, bf16, BH * NC, st) != cudaSuccess) return GDN2_ERR_CUDA;
+  if (timed(GDN2_K_BWD_PRE, st, [&] { return launch_bwd_pre(bp, bf16, BH * NC, st); }) != cudaSuccess)
+    return GDN2_ERR_CUDA;
 
   ScanParams sp{};
   sp.img = bp.op.res + bp.op.rl.mb;
@@ -145,8 +208,9 @@ extern "C" gdn2_status gdn2_bwd(const gdn2_desc* d, const void* q, const void* k
   sp.reverse = 1;
   sp.clip = d->clip;
   sp.status = dev_status;
-  if (launch_scan(sp, BH, st) != cudaSuccess) return GDN2_ERR_CUDA;
+  if (timed(GDN2_K_BWD_SCAN, st, [&] { return launch_scan(sp, BH, st); }) != cudaSuccess) return GDN2_ERR_CUDA;
 
-  if (launch_bwd_intra(bp, bf16, BH * NC, st) != cudaSuccess) return GDN2_ERR_CUDA;
+  if (timed(GDN2_K_BWD_INTRA, st, [&] { return launch_bwd_intra(bp, bf16, BH * NC, st); }) != cudaSuccess)
+    return GDN2_ERR_CUDA;
   return GDN2_OK;
 }

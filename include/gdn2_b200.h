@@ -124,6 +124,21 @@ const char* gdn2_status_string(gdn2_status status);
 gdn2_status gdn2_selftest_gemm(const float* A, const float* B, float* C, int32_t N, int32_t precision,
                                int32_t a_mode, int32_t b_mn, uint32_t* dev_status, void* stream);
 
+/* Profiling hook (no counterpart in the reference).  While enabled, every kernel launch of
+ * gdn2_fwd / gdn2_bwd is bracketed by CUDA events recorded on the caller's stream.
+ * gdn2_profile_collect synchronises on those events, writes per-kernel summed milliseconds and
+ * launch counts for kernel ids [0, n) (GDN2_K_*), clears the record and returns the number of
+ * timed launches. */
+#define GDN2_K_FWD_INTRA 0
+#define GDN2_K_FWD_SCAN 1
+#define GDN2_K_FWD_OUT 2
+#define GDN2_K_BWD_PRE 3
+#define GDN2_K_BWD_SCAN 4
+#define GDN2_K_BWD_INTRA 5
+#define GDN2_K_COUNT 6
+void gdn2_profile_enable(int32_t enable);
+int32_t gdn2_profile_collect(float* ms, int32_t* counts, int32_t n);
+
 #ifdef __cplusplus
 }
 #endif
