@@ -36,7 +36,8 @@ class Gdn2Desc(ctypes.Structure):
 
 
 EXPORTS = ("gdn2_residual_bytes", "gdn2_bwd_workspace_bytes", "gdn2_fwd", "gdn2_bwd",
-           "gdn2_status_string", "gdn2_selftest_gemm", "gdn2_profile_enable", "gdn2_profile_collect")
+           "gdn2_status_string", "gdn2_selftest_gemm", "gdn2_profile_enable", "gdn2_profile_collect",
+           "gdn2_fwd_noalloc")
 # kernel ids of gdn2_profile_collect
 KERNELS = ("fwd_intra", "fwd_scan", "fwd_out", "bwd_pre", "bwd_scan", "bwd_intra")
 
@@ -59,6 +60,8 @@ def _declare(lib):
     lib.gdn2_profile_enable.argtypes = [ctypes.c_int32]
     lib.gdn2_profile_collect.restype = ctypes.c_int32
     lib.gdn2_profile_collect.argtypes = [P, P, ctypes.c_int32]
+    lib.gdn2_fwd_noalloc.restype = ctypes.c_int
+    lib.gdn2_fwd_noalloc.argtypes = [ctypes.POINTER(Gdn2Desc)] + [P] * 11
     return lib
 
 

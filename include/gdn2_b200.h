@@ -124,6 +124,24 @@ const char* gdn2_status_string(gdn2_status status);
 gdn2_status gdn2_selftest_gemm(const float* A, const float* B, float* C, int32_t N, int32_t precision,
                                int32_t a_mode, int32_t b_mn, uint32_t* dev_status, void* stream);
 
+/* Allocation-free forward (no counterpart in the reference).  Same arguments and results as
+ * gdn2_fwd minus the residual buffer: the scratch lives in a fixed 64 MiB device array inside the
+ * library, so the call performs no device allocation.  It is meant for callers that cannot
+ * allocate at the point where they run the operator, such as runtime plugin / custom-call hooks
+ * whose device memory is owned and planned by the host framework's allocator, and which receive
+ * only a stream plus their input and output pointers.
+ *   Limit: gdn2_residual_bytes(desc) must be <= 64 MiB (about 96 chunk-heads of 128 tokens in
+ *   the default modes, e.g. B=1, H=6, L=2048); larger problems are rejected with
+ *   GDN2_ERR_INVALID_ARGUMENT before any launch.
+ *   The first call on each device looks up the array's device address (cudaGetSymbolAddress);
+ *   make that first call before any stream capture.
+ *   All calls on a device share the one array: calls that overlap on the GPU (different streams
+ *   without ordering) race on it.  No state carries from one call to the next.
+ *   Forward only: there is no residual to hand to gdn2_bwd. */
+gdn2_status gdn2_fwd_noalloc(const gdn2_desc* desc, const void* q, const void* k, const void* v, const void* w,
+                             const void* b, const void* g, const float* h0, float* o, float* h_final,
+                             uint32_t* dev_status, void* stream);
+
 /* Profiling hook (no counterpart in the reference).  While enabled, every kernel launch of
  * gdn2_fwd / gdn2_bwd is bracketed by CUDA events recorded on the caller's stream.
  * gdn2_profile_collect synchronises on those events, writes per-kernel summed milliseconds and
