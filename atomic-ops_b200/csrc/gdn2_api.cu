@@ -58,7 +58,7 @@ OpParams make_params(const gdn2_desc* d, const void* q, const void* k, const voi
   p.b3_mode = d->b3_dot_mode;
   p.status = status;
   p.res = static_cast<uint8_t*>(residual);
-  p.rl = res_layout(d->B * d->H, p.NC, mode_from_enum(d->dot_mode), mode_from_enum(d->b3_dot_mode));
+  p.rl = res_layout(d->B * d->H, p.NC, mode_from_enum(d->dot_mode));
   return p;
 }
 
@@ -123,12 +123,12 @@ extern "C" int32_t gdn2_profile_collect(float* ms, int32_t* counts, int32_t n) {
 
 extern "C" size_t gdn2_residual_bytes(const gdn2_desc* d) {
   if (check_desc(d) != GDN2_OK) return 0;
-  return res_layout(d->B * d->H, d->L / d->bt, mode_from_enum(d->dot_mode), mode_from_enum(d->b3_dot_mode)).total;
+  return res_layout(d->B * d->H, d->L / d->bt, mode_from_enum(d->dot_mode)).total;
 }
 
 extern "C" size_t gdn2_bwd_workspace_bytes(const gdn2_desc* d) {
   if (check_desc(d) != GDN2_OK) return 0;
-  return ws_layout(d->B * d->H, d->L / d->bt).total;
+  return ws_layout(d->B * d->H, d->L / d->bt, mode_from_enum(d->b3_dot_mode)).total;
 }
 
 extern "C" gdn2_status gdn2_fwd(const gdn2_desc* d, const void* q, const void* k, const void* v, const void* w,
@@ -189,14 +189,14 @@ extern "C" gdn2_status gdn2_bwd(const gdn2_desc* d, const void* q, const void* k
   bp.dq = dq; bp.dk = dk; bp.dv = dv; bp.dw = dw; bp.db = db; bp.dg = dg;
   bp.ws = static_cast<uint8_t*>(workspace);
   const int BH = d->B * d->H, NC = bp.op.NC;
-  bp.wl = ws_layout(BH, NC);
+  bp.wl = ws_layout(BH, NC, mode_from_enum(d->b3_dot_mode));
 
   if (timed(GDN2_K_BWD_PRE, st, [&] { return launch_bwd_pre(bp, bf16, BH * NC, st); }) != cudaSuccess)
     return GDN2_ERR_CUDA;
 
   ScanParams sp{};
-  sp.img = bp.op.res + bp.op.rl.mb;
-  sp.img_stride = bp.op.rl.mb_stride;
+  sp.img = bp.ws + bp.wl.mb;
+  sp.img_stride = bp.wl.mb_stride;
   sp.add = reinterpret_cast<const float*>(bp.ws + bp.wl.cc);
   sp.state_in = d_hfinal;
   sp.states = reinterpret_cast<float*>(bp.ws + bp.wl.dhs);

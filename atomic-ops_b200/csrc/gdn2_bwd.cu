@@ -32,7 +32,8 @@ __device__ __forceinline__ uint8_t* align1024b(uint8_t* p) {
 }
 
 // ---------------------------------------------------------------------------------------
-// bwd_pre: dvl = Aqk^T do,  Cc = scale qg^T do - wp^T dvl      (b3_dot_mode, mega.py:31-34)
+// bwd_pre: dvl = Aqk^T do,  Cc = scale qg^T do - wp^T dvl, and the transposed transition
+// image M^T = diag(e^gl) - wp^T kg of the reverse scan      (b3_dot_mode, mega.py:31-34)
 // ---------------------------------------------------------------------------------------
 template <class TIn>
 __global__ void __launch_bounds__(kThreads, 1) bwd_pre_kernel(const BwdParams P) {
@@ -48,6 +49,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_pre_kernel(const BwdParams P)
   const int ch = blockIdx.x, bh = ch / p.NC, c = ch % p.NC;
   const long long off = chunk_off(p, bh, c);
   const TIn* q = reinterpret_cast<const TIn*>(p.q) + off;
+  const TIn* k = reinterpret_cast<const TIn*>(p.k) + off;
   const TIn* g = reinterpret_cast<const TIn*>(p.g) + off;
   const float* do_ = P.d_o + off;
   const size_t mat = (size_t)kT * kD;
@@ -55,6 +57,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_pre_kernel(const BwdParams P)
   const float* wp_g = reinterpret_cast<const float*>(p.res + p.rl.wp) + (size_t)ch * mat;
   float* dvl_g = reinterpret_cast<float*>(P.ws + P.wl.dvl) + (size_t)ch * mat;
   float* cc_g = reinterpret_cast<float*>(P.ws + P.wl.cc) + (size_t)ch * mat;
+  uint8_t* mb_g = P.ws + P.wl.mb + (size_t)ch * P.wl.mb_stride;
   const Mode m3 = mode_from_enum(p.b3_mode);
   const float clip = p.clip, scale = p.scale;
 
@@ -86,23 +89,43 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_pre_kernel(const BwdParams P)
 #pragma unroll
     for (int j = 0; j < 32; ++j) x[j] = scale * sanitize(x[j] * ex(fminf(gr[j], 0.f)), clip);
   };
+  auto src_kg = [&](int r, int c0, float* x) {  // sanitize(k e^min(gl - gc, 0))
+    ld32_in(k + r * kD + c0, x);
+    const float* gr = gcs + r * kGcPitch + c0;
+    const float* gl = gcs + (kT - 1) * kGcPitch + c0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) x[j] = sanitize(x[j] * ex(fminf(gl[j] - gr[j], 0.f)), clip);
+  };
   auto src_wp = [&](int r, int c0, float* x) { ld32_f(wp_g + r * kD + c0, x); };
-  auto src_s0 = [&](int, int c0, float* x) { tmem_ld32(S0, (uint32_t)c0, x); };
+  auto tm0 = [&](int, int c0, float* x) { tmem_ld32(S0, (uint32_t)c0, x); };
 
   // S0 = Aqk^T do, S1 = (scale qg)^T do   (shared B = do)
-  gemm_pairs(m3, pool, mb, S0, true, src_aqk, true, src_do, false, false, 2, S1, true, src_qg, true, src_do, false,
-             false, false, true);
+  gemm2(m3, pool, mb, S0, mn_any(src_aqk), mn_any(src_do), false, false, S1, mn_any(src_qg), mn_any(NoSrc()), false,
+        false, false, true);
   for (int c0 = 0; c0 < kD; c0 += 32) {
     float x[32];
     tmem_ld32(S0, c0, x);
     st32_f(dvl_g + t * kD + c0, x);
   }
   // S1 -= wp^T dvl
-  gemm_pairs(m3, pool, mb, S1, true, src_wp, true, src_s0, true, true);
+  gemm1(m3, pool, mb, S1, mn_any(src_wp), mn_own(tm0), true, true);
   for (int c0 = 0; c0 < kD; c0 += 32) {
     float x[32];
     tmem_ld32(S1, c0, x);
     st32_f(cc_g + t * kD + c0, x);
+  }
+  // transposed transition of this chunk for the reverse scan: M^T = diag(e^gl) - wp^T kg
+  gemm1(m3, pool, mb, S0, mn_any(src_wp), mn_any(src_kg), false, false);
+  {
+    const float dec = ex(fminf(gcs[(kT - 1) * kGcPitch + t], 0.f));
+    for (int c0 = 0; c0 < kD; c0 += 32) {
+      float x[32];
+      tmem_ld32(S0, c0, x);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) x[j] = ((c0 + j) == t ? dec : 0.f) - x[j];
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) image_store8(mb_g, m3, t, c0 + j, x + j);
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -253,7 +276,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_intra_kernel(const BwdParams 
   };
 
   // 1. S0 = dv_new = sanitize(dvl + kg dh_next)                                  [B1, b3 mode]
-  gemm_pairs(m3, pool, mb, S0, false, src_kg, true, src_dhn, false, false);
+  gemm1(m3, pool, mb, S0, kmaj(src_kg), mn_any(src_dhn), false, false);
   for (int c0 = 0; c0 < kD; c0 += 32) {
     float x[32], y[32];
     tmem_ld32(S0, c0, x);
@@ -263,10 +286,10 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_intra_kernel(const BwdParams 
     tmem_st32(S0, c0, x);
   }
   // 2. S1 = dwp' = -dv_new (e^m h_pre)^T                                          [B3]
-  gemm_pairs(m3, pool, mb, S1, false, tm(S0), false, src_hpre_em, true, false);
+  gemm1(m3, pool, mb, S1, kmaj(tm(S0)), kmaj(src_hpre_em), true, false);
   // 3. S2 = dA = sanitize(dwp' (bk E)^T + dv_new (w v)^T)                          [B3]
-  gemm_pairs(m3, pool, mb, S2, false, tm(S1), false, src_bkE, false, false, 2, S2, false, tm(S0), false, src_wv,
-             false, true);
+  gemm2(m3, pool, mb, S2, kmaj(tm(S1)), kmaj(src_bkE), false, false, S2, kmaj(tm(S0)), kmaj(src_wv), false, true,
+        false, false);
   for (int c0 = 0; c0 < kT; c0 += 32) {
     float x[32];
     tmem_ld32(S2, c0, x);
@@ -275,7 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_intra_kernel(const BwdParams 
     tmem_st32(S2, c0, x);
   }
   // 4. S3 = dwv = A^T dv_new;  dw = dwv v, dv = dwv w                              [B3]
-  gemm_pairs(m3, pool, mb, S3, true, src_ainv, true, tm(S0), false, false);
+  gemm1(m3, pool, mb, S3, mn_any(src_ainv), mn_own(tm(S0)), false, false);
   for (int c0 = 0; c0 < kD; c0 += 32) {
     float x[32], a[32], y[32];
     tmem_ld32(S3, c0, x);
@@ -289,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_intra_kernel(const BwdParams 
     st32_out(dv + t * kD + c0, y);
   }
   // 5. S0 = tmp = sanitize(dA A^T)                                                   [B3]
-  gemm_pairs(m3, pool, mb, S0, false, tm(S2), false, src_ainv, false, false);
+  gemm1(m3, pool, mb, S0, kmaj(tm(S2)), kmaj(src_ainv), false, false);
   for (int c0 = 0; c0 < kT; c0 += 32) {
     float x[32];
     tmem_ld32(S0, c0, x);
@@ -298,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_intra_kernel(const BwdParams 
     tmem_st32(S0, c0, x);
   }
   // 6. S2 = dAkk = sanitize(-(1-eps) A^T tmp) strict                                  [B3]
-  gemm_pairs(m3, pool, mb, S2, true, src_ainv, true, tm(S0), true, false);
+  gemm1(m3, pool, mb, S2, mn_any(src_ainv), mn_own(tm(S0)), true, false);
   {
     const float keep = 1.0f - p.eps;
     for (int c0 = 0; c0 < kT; c0 += 32) {
@@ -310,10 +333,10 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_intra_kernel(const BwdParams 
     }
   }
   // 7. S0 = A^T dwp' (B3)  +  dAkk (k F) (B4, highest)
-  gemm_pairs(m3, pool, mb, S0, true, src_ainv, true, tm(S1), false, false);
-  gemm_pairs(mh, pool, mb, S0, false, tm(S2), true, src_kF, false, true);
+  gemm1(m3, pool, mb, S0, mn_any(src_ainv), mn_own(tm(S1)), false, false);
+  gemm1(mh, pool, mb, S0, kmaj(tm(S2)), mn_any(src_kF), false, true);
   // 8. S1 = dAqk = (do v_new^T) causal                                              [B2]
-  gemm_pairs(m3, pool, mb, S1, false, src_do, false, src_vnew, false, false);
+  gemm1(m3, pool, mb, S1, kmaj(src_do), kmaj(src_vnew), false, false);
   for (int c0 = 0; c0 < kT; c0 += 32) {
     float x[32];
     tmem_ld32(S1, c0, x);
@@ -322,8 +345,8 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_intra_kernel(const BwdParams 
     tmem_st32(S1, c0, x);
   }
   // 9. S3 = scale do (e^m h_pre)^T (B3)  +  scale dAqk (k F) (B4)
-  gemm_pairs(m3, pool, mb, S3, false, src_do_s, false, src_hpre_em, false, false);
-  gemm_pairs(mh, pool, mb, S3, false, tm_scaled(S1), true, src_kF, false, true);
+  gemm1(m3, pool, mb, S3, kmaj(src_do_s), kmaj(src_hpre_em), false, false);
+  gemm1(mh, pool, mb, S3, kmaj(tm_scaled(S1)), mn_any(src_kF), false, true);
   // 10.-11. finish dq and db;  S3 <- dgc partial;  S0 <- Dbk b E (pre-scaled dk partial)
   {
     const float* gr = gcrow(t);
@@ -358,9 +381,9 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_intra_kernel(const BwdParams 
     }
   }
   // 12. S0 += v_new (e^(gl-m) dh_next)^T (B3)  +  scale dAqk^T (q E) + dAkk^T (bk E) (B4)
-  gemm_pairs(m3, pool, mb, S0, false, src_vnew, false, src_dhn_gl, false, true);
-  gemm_pairs(mh, pool, mb, S0, true, tm(S1), true, src_qE, false, true, 2, S0, true, tm(S2), true, src_bkE, false,
-             true);
+  gemm1(m3, pool, mb, S0, kmaj(src_vnew), kmaj(src_dhn_gl), false, true);
+  gemm2(mh, pool, mb, S0, mn_own(tm(S1)), mn_any(src_qE), false, true, S0, mn_own(tm(S2)), mn_any(src_bkE), false,
+        true, false, false);
   // 13. dk = F o S0;  dgc = S3 - k o dk (+ decay term on the last row);  dgc -> smem (gcs rows)
   {
     float* gr = gcs + t * kGcPitch;

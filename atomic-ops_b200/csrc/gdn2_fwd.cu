@@ -38,21 +38,6 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
 
-// Load 8 consecutive input values (row-major T x D chunk) as fp32.
-template <class TIn>
-__device__ __forceinline__ void ld8(const TIn* p, float v[8]) {
-  ld4(p, v);
-  ld4(p + 4, v + 4);
-}
-__device__ __forceinline__ void ld8f(const float* p, float v[8]) {
-  float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
-  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-}
-__device__ __forceinline__ void st8f(float* p, const float v[8]) {
-  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
-  *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
-}
-
 // ---------------------------------------------------------------------------------------
 // fwd_intra
 // ---------------------------------------------------------------------------------------
@@ -84,12 +69,9 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_intra_kernel(const OpParams p
   float* u_g = reinterpret_cast<float*>(p.res + p.rl.u) + (size_t)ch * mat;
   float* bc_g = reinterpret_cast<float*>(p.res + p.rl.bc) + (size_t)ch * mat;
   uint8_t* mf_g = p.res + p.rl.mf + (size_t)ch * p.rl.mf_stride;
-  uint8_t* mb_g = p.res + p.rl.mb + (size_t)ch * p.rl.mb_stride;
 
   const Mode md = mode_from_enum(p.dot_mode);
   const Mode ms = mode_from_enum(p.solve_mode);
-  const Mode mfm = mode_from_enum(p.dot_mode);  // forward scan image mode
-  const Mode mbm = mode_from_enum(p.b3_mode);   // backward scan image mode
   const float clip = p.clip;
 
   if (warp == 0) {
@@ -115,45 +97,72 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_intra_kernel(const OpParams p
   const uint32_t tb = *tslot;
   const uint32_t S0 = tb, S1 = tb + 128, S2 = tb + 256, S3 = tb + 384;
   MmaBar mbar{bar, 0u, p.status};
-  const float* gct = gcs + t * kGcPitch;  // this thread's row of gc
 
-  // ---- 1. scores: S0 = Qt Kt^T, S1 = BKt Kt^T ------------------------------------------
-  {
-    const int KS = kslice(md), ns = kD / KS;
-    const bool lo = md.passes == 3;
-    for (int s = 0; s < ns; ++s) {
-      const Tile A1[2] = {pool_k(pool, 0), pool_k(pool, 1)};
-      const Tile A2[2] = {pool_k(pool, 2), pool_k(pool, 3)};
-      const Tile Bt[2] = {pool_k(pool, 4), pool_k(pool, 5)};
-      for (int i = 0; i < KS; i += 8) {
-        const int d0 = s * KS + i;
-        float qv[8], kv[8], bv[8], vq[8], vb[8], vk[8];
-        ld8(q + t * kD + d0, qv);
-        ld8(k + t * kD + d0, kv);
-        ld8(b + t * kD + d0, bv);
+  // ---- row sources (row r; global / shared-memory sources may be called for any row) ----
+  auto src_qE = [&](int r, int c0, float* x) {  // q e^(gc - m)
+    ld32_in(q + r * kD + c0, x);
+    const float* gr = gcs + r * kGcPitch + c0;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float e = gct[d0 + j] - mid_s[d0 + j];
-          const float a = ex(e), ia = ex(-e);
-          vq[j] = qv[j] * a;
-          vb[j] = bv[j] * kv[j] * a;
-          vk[j] = kv[j] * ia;
-        }
-        stage_krow(A1[0], A1[1], lo, md.fmt, t, i, vq, 8);
-        stage_krow(A2[0], A2[1], lo, md.fmt, t, i, vb, 8);
-        stage_krow(Bt[0], Bt[1], lo, md.fmt, t, i, vk, 8);
-      }
-      staged_sync();
-      if (t == 0) {
-        tc_fence_after();
-        issue_slice(md, S0, A1, Bt, 128, false, s > 0);
-        issue_slice(md, S1, A2, Bt, 128, false, s > 0);
-      }
-      mbar.commit_wait();
+    for (int j = 0; j < 32; ++j) x[j] *= ex(gr[j] - mid_s[c0 + j]);
+  };
+  auto src_bkE = [&](int r, int c0, float* x) {  // b k e^(gc - m)
+    float kv[32];
+    ld32_in(b + r * kD + c0, x);
+    ld32_in(k + r * kD + c0, kv);
+    const float* gr = gcs + r * kGcPitch + c0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) x[j] = x[j] * kv[j] * ex(gr[j] - mid_s[c0 + j]);
+  };
+  auto src_kF = [&](int r, int c0, float* x) {  // k e^(m - gc)
+    ld32_in(k + r * kD + c0, x);
+    const float* gr = gcs + r * kGcPitch + c0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) x[j] *= ex(mid_s[c0 + j] - gr[j]);
+  };
+  auto src_kb = [&](int r, int c0, float* x) {  // b k e^min(gc, 0)
+    float kv[32];
+    ld32_in(b + r * kD + c0, x);
+    ld32_in(k + r * kD + c0, kv);
+    const float* gr = gcs + r * kGcPitch + c0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) x[j] = x[j] * kv[j] * ex(fminf(gr[j], 0.f));
+  };
+  auto src_wv = [&](int r, int c0, float* x) {
+    float vv[32];
+    ld32_in(w + r * kD + c0, x);
+    ld32_in(v + r * kD + c0, vv);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) x[j] *= vv[j];
+  };
+  auto src_kg = [&](int r, int c0, float* x) {  // sanitize(k e^min(gl - gc, 0))
+    ld32_in(k + r * kD + c0, x);
+    const float* gr = gcs + r * kGcPitch + c0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) x[j] = sanitize(x[j] * ex(fminf(gl_s[c0 + j] - gr[j], 0.f)), clip);
+  };
+  auto src_dinv = [&](int r, int c0, float* x) {  // row r of the block-diagonal Dg^-1
+    if ((c0 >> 5) == (r >> 5)) {
+      const float* src = dsm + (r >> 5) * 1056 + (r & 31) * 33;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) x[j] = src[j];
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) x[j] = 0.f;
     }
-  }
+  };
+  auto src_R = [&](int r, int c0, float* x) {  // strictly block-lower part of Se (TMEM S1, owner)
+    tmem_ld32(S1, (uint32_t)c0, x);
+    const int lim = (r >> 5) << 5;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) x[j] = (c0 + j < lim) ? x[j] : 0.f;
+  };
+  auto tm = [&](uint32_t slot) { return [=](int, int c0, float* x) { tmem_ld32(slot, (uint32_t)c0, x); }; };
 
-  // ---- 2. Aqk out (scale, causal, sanitize); Se = (1-eps) sanitize(Akk) strict, in place --
+  // ---- 1. scores: S0 = (q E)(k F)^T, S1 = (b k E)(k F)^T                      (dot mode) --------
+  gemm2(md, pool, mbar, S0, kmaj(src_qE), kmaj(src_kF), false, false, S1, kmaj(src_bkE), kmaj(NoSrc()), false,
+        false, false, true);
+
+  // ---- 2. Aqk out (scale, causal, sanitize); Se = (1-eps) sanitize(Akk) strict, in place -----------
   {
     const float keep = 1.0f - p.eps;
     const int blk = t >> 5;
@@ -162,8 +171,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_intra_kernel(const OpParams p
       tmem_ld32(S0, c0, x);
 #pragma unroll
       for (int j = 0; j < 32; ++j) x[j] = (c0 + j <= t) ? sanitize(p.scale * x[j], clip) : 0.f;
-#pragma unroll
-      for (int j = 0; j < 32; j += 8) st8f(aqk_g + t * kT + c0 + j, x + j);
+      st32_f(aqk_g + t * kT + c0, x);
       tmem_ld32(S1, c0, x);
 #pragma unroll
       for (int j = 0; j < 32; ++j) x[j] = (c0 + j < t) ? keep * sanitize(x[j], clip) : 0.f;
@@ -178,7 +186,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_intra_kernel(const OpParams p
   __syncthreads();
   tc_fence_after();
 
-  // ---- 3. diagonal-block inverses (forward substitution, warp = block, lane = column) ----
+  // ---- 3. diagonal-block inverses (forward substitution, warp = block, lane = column) ----------
   {
     const float* Sb = dsm + warp * 1056;
     float x[32];
@@ -195,190 +203,51 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_intra_kernel(const OpParams p
   }
   __syncthreads();
 
-  // Row r of Dg^-1 (block-diagonal), columns [c0, c0+8).
-  auto dinv_row8 = [&](int r, int c0, float* out) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int col = c0 + j;
-      out[j] = ((col >> 5) == (r >> 5)) ? dsm[(r >> 5) * 1056 + (r & 31) * 33 + (col & 31)] : 0.f;
-    }
-  };
-
-  // Generic solve-mode product D = X Y with X given row-wise (K-major source, thread = row of X)
-  // and Y given row-wise (MN-major source, thread = row of Y = k).
-  //   xrow(t, k0, out8): 8 values of row t of X at columns k0..k0+7
-  //   yrow32(j, c0, out32): 32 values of row j of Y at columns c0..c0+31 (warp-collective)
-  auto solve_gemm = [&](uint32_t dcol, auto xrow, auto yrow32) {
-    const int KS = kslice(ms), ns = kT / KS;
-    const bool lo = ms.passes == 3;
-    for (int s = 0; s < ns; ++s) {
-      const int k0 = s * KS;
-      const Tile At[2] = {pool_k(pool, 0), pool_k(pool, 1)};
-      const Tile Bt[2] = {pool_mn(pool, 2, ms), pool_mn(pool, 3, ms)};
-      for (int i = 0; i < KS; i += 8) {
-        float xv[8];
-        xrow(t, k0 + i, xv);
-        stage_krow(At[0], At[1], lo, ms.fmt, t, i, xv, 8);
-      }
-      if (warp * 32 >= k0 && warp * 32 < k0 + KS) {
-        for (int c0 = 0; c0 < kT; c0 += 32) {
-          float yv[32];
-          yrow32(t, c0, yv);
-#pragma unroll
-          for (int j = 0; j < 32; j += 8) stage_mnrow(Bt[0], Bt[1], lo, ms.fmt, t - k0, c0 + j, yv + j, 8);
-        }
-      }
-      staged_sync();
-      if (t == 0) {
-        tc_fence_after();
-        issue_slice(ms, dcol, At, Bt, 128, false, s > 0);
-      }
-      mbar.commit_wait();
-    }
-  };
-  auto tm_row8 = [&](uint32_t col0) {  // K-major source rows from a TMEM slot
-    return [=](int, int k0, float* out) {
-      float x[32];
-      tmem_ld32(col0, (uint32_t)(k0 & ~31), x);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) out[j] = x[(k0 & 31) + j];
-    };
-  };
-  auto tm_row32 = [&](uint32_t col0) {
-    return [=](int, int c0, float* out) { tmem_ld32(col0, (uint32_t)c0, out); };
-  };
-
-  // ---- 4. W = Dg^-1 R  -> S0 ---------------------------------------------------------------
-  solve_gemm(S0, [&](int r, int k0, float* out) { dinv_row8(r, k0, out); },
-             [&](int j, int c0, float* out) {
-               tmem_ld32(S1, (uint32_t)c0, out);
-               const int lim = (j >> 5) << 5;  // strictly block-lower part only
-#pragma unroll
-               for (int i = 0; i < 32; ++i) out[i] = (c0 + i < lim) ? out[i] : 0.f;
-             });
-  // ---- 5. W2 = W W -> S2 ---------------------------------------------------------------------
-  solve_gemm(S2, tm_row8(S0), tm_row32(S0));
-  // ---- 6. P = W2 Dg^-1 + Dg^-1 -> S3 -----------------------------------------------------------
-  solve_gemm(S3, tm_row8(S2), [&](int j, int c0, float* out) {
-#pragma unroll
-    for (int i = 0; i < 32; i += 8) dinv_row8(j, c0 + i, out + i);
-  });
-  for (int c0 = 0; c0 < kT; c0 += 32) {
-    float x[32];
+  // ---- 4.-7. A = (I - W)(I + W^2) Dg^-1,  W = Dg^-1 R                          (solve mode) --------
+  gemm1(ms, pool, mbar, S0, kmaj(src_dinv), mn_own(src_R), false, false);   // W -> S0
+  gemm1(ms, pool, mbar, S2, kmaj(tm(S0)), mn_own(tm(S0)), false, false);    // W^2 -> S2
+  gemm1(ms, pool, mbar, S3, kmaj(tm(S2)), mn_any(src_dinv), false, false);  // W^2 Dg^-1 -> S3
+  for (int c0 = 0; c0 < kT; c0 += 32) {                                      // P = S3 + Dg^-1
+    float x[32], dv[32];
     tmem_ld32(S3, c0, x);
-    if ((c0 >> 5) == (t >> 5)) {
+    src_dinv(t, c0, dv);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) x[j] += dsm[(t >> 5) * 1056 + (t & 31) * 33 + j];
-    }
+    for (int j = 0; j < 32; ++j) x[j] += dv[j];
     tmem_st32(S3, c0, x);
   }
-  // ---- 7. WP = W P -> S2;  A = sanitize(P - WP) -> S1 and the residual ------------------------
-  solve_gemm(S2, tm_row8(S0), tm_row32(S3));
-  for (int c0 = 0; c0 < kT; c0 += 32) {
+  gemm1(ms, pool, mbar, S2, kmaj(tm(S0)), mn_own(tm(S3)), false, false);    // W P -> S2
+  for (int c0 = 0; c0 < kT; c0 += 32) {                                      // A = sanitize(P - W P)
     float x[32], y[32];
     tmem_ld32(S3, c0, x);
     tmem_ld32(S2, c0, y);
 #pragma unroll
     for (int j = 0; j < 32; ++j) x[j] = (c0 + j <= t) ? sanitize(x[j] - y[j], clip) : 0.f;
     tmem_st32(S1, c0, x);
-#pragma unroll
-    for (int j = 0; j < 32; j += 8) st8f(ainv_g + t * kT + c0 + j, x + j);
+    st32_f(ainv_g + t * kT + c0, x);
   }
 
-  // ---- 8. wp = A (b k e^gc) -> S0,  u = A (w v) -> S2   (dot mode) ----------------------------
-  {
-    const int KS = kslice(md), ns = kT / KS;
-    const bool lo = md.passes == 3;
-    for (int s = 0; s < ns; ++s) {
-      const int k0 = s * KS;
-      const Tile At[2] = {pool_k(pool, 0), pool_k(pool, 1)};
-      const Tile B1[2] = {pool_mn(pool, 2, md), pool_mn(pool, 3, md)};
-      const Tile B2[2] = {pool_mn(pool, 4, md), pool_mn(pool, 5, md)};
-      for (int i = 0; i < KS; i += 32) {
-        float x[32];
-        tmem_ld32(S1, (uint32_t)(k0 + i), x);
+  // ---- 8. wp = A (b k e^gc) -> S0,  u = A (w v) -> S2                          (dot mode) --------
+  gemm2(md, pool, mbar, S0, kmaj(tm(S1)), mn_any(src_kb), false, false, S2, kmaj(NoSrc()), mn_any(src_wv), false,
+        false, true, false);
+  for (int c0 = 0; c0 < kD; c0 += 32) {
+    float x[32];
+    tmem_ld32(S0, c0, x);
 #pragma unroll
-        for (int j = 0; j < 32; j += 8) stage_krow(At[0], At[1], lo, md.fmt, t, i + j, x + j, 8);
-      }
-      if (warp * 32 >= k0 && warp * 32 < k0 + KS) {
-        for (int c0 = 0; c0 < kD; c0 += 8) {
-          float kv[8], bv[8], wv[8], vv[8], kb[8], wvv[8];
-          ld8(k + t * kD + c0, kv);
-          ld8(b + t * kD + c0, bv);
-          ld8(w + t * kD + c0, wv);
-          ld8(v + t * kD + c0, vv);
+    for (int j = 0; j < 32; ++j) x[j] = sanitize(x[j], clip);
+    tmem_st32(S0, c0, x);
+    st32_f(wp_g + t * kD + c0, x);
+    tmem_ld32(S2, c0, x);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            kb[j] = bv[j] * kv[j] * ex(fminf(gct[c0 + j], 0.f));
-            wvv[j] = wv[j] * vv[j];
-          }
-          stage_mnrow(B1[0], B1[1], lo, md.fmt, t - k0, c0, kb, 8);
-          stage_mnrow(B2[0], B2[1], lo, md.fmt, t - k0, c0, wvv, 8);
-        }
-      }
-      staged_sync();
-      if (t == 0) {
-        tc_fence_after();
-        issue_slice(md, S0, At, B1, 128, false, s > 0);
-        issue_slice(md, S2, At, B2, 128, false, s > 0);
-      }
-      mbar.commit_wait();
-    }
-    for (int c0 = 0; c0 < kD; c0 += 32) {
-      float x[32];
-      tmem_ld32(S0, c0, x);
-#pragma unroll
-      for (int j = 0; j < 32; ++j) x[j] = sanitize(x[j], clip);
-      tmem_st32(S0, c0, x);
-#pragma unroll
-      for (int j = 0; j < 32; j += 8) st8f(wp_g + t * kD + c0 + j, x + j);
-      tmem_ld32(S2, c0, x);
-#pragma unroll
-      for (int j = 0; j < 32; ++j) x[j] = sanitize(x[j], clip);
-      tmem_st32(S2, c0, x);
-#pragma unroll
-      for (int j = 0; j < 32; j += 8) st8f(u_g + t * kD + c0 + j, x + j);
-    }
+    for (int j = 0; j < 32; ++j) x[j] = sanitize(x[j], clip);
+    tmem_st32(S2, c0, x);
+    st32_f(u_g + t * kD + c0, x);
   }
 
-  // ---- 9. M = diag(e^gl) - kg^T wp -> S1,  Bc = kg^T u -> S3   (dot mode) ----------------------
+  // ---- 9. M = diag(e^gl) - kg^T wp -> S1,  Bc = kg^T u -> S3                  (dot mode) --------
+  gemm2(md, pool, mbar, S1, mn_any(src_kg), mn_own(tm(S0)), false, false, S3, mn_any(NoSrc()), mn_own(tm(S2)),
+        false, false, true, false);
   {
-    const int KS = kslice(md), ns = kT / KS;
-    const bool lo = md.passes == 3;
-    for (int s = 0; s < ns; ++s) {
-      const int k0 = s * KS;
-      const Tile At[2] = {pool_mn(pool, 0, md), pool_mn(pool, 1, md)};
-      const Tile B1[2] = {pool_mn(pool, 2, md), pool_mn(pool, 3, md)};
-      const Tile B2[2] = {pool_mn(pool, 4, md), pool_mn(pool, 5, md)};
-      if (warp * 32 >= k0 && warp * 32 < k0 + KS) {
-        for (int c0 = 0; c0 < kD; c0 += 32) {
-          float x[32];
-          float kv[8];
-#pragma unroll
-          for (int j = 0; j < 32; j += 8) {
-            ld8(k + t * kD + c0 + j, kv);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) x[j + i] = sanitize(kv[i] * ex(fminf(gl_s[c0 + j + i] - gct[c0 + j + i], 0.f)), clip);
-          }
-#pragma unroll
-          for (int j = 0; j < 32; j += 8) stage_mnrow(At[0], At[1], lo, md.fmt, t - k0, c0 + j, x + j, 8);
-          tmem_ld32(S0, (uint32_t)c0, x);
-#pragma unroll
-          for (int j = 0; j < 32; j += 8) stage_mnrow(B1[0], B1[1], lo, md.fmt, t - k0, c0 + j, x + j, 8);
-          tmem_ld32(S2, (uint32_t)c0, x);
-#pragma unroll
-          for (int j = 0; j < 32; j += 8) stage_mnrow(B2[0], B2[1], lo, md.fmt, t - k0, c0 + j, x + j, 8);
-        }
-      }
-      staged_sync();
-      if (t == 0) {
-        tc_fence_after();
-        issue_slice(md, S1, At, B1, 128, false, s > 0);
-        issue_slice(md, S3, At, B2, 128, false, s > 0);
-      }
-      mbar.commit_wait();
-    }
-    // Row d = t of M and Bc.
+    const Mode mfm = md;  // the forward scan multiplies in dot mode
     const float dec = ex(fminf(gl_s[t], 0.f));
     for (int c0 = 0; c0 < kD; c0 += 32) {
       float x[32];
@@ -387,11 +256,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_intra_kernel(const OpParams p
       for (int j = 0; j < 32; ++j) x[j] = ((c0 + j) == t ? dec : 0.f) - x[j];
 #pragma unroll
       for (int j = 0; j < 32; j += 8) image_store8(mf_g, mfm, t, c0 + j, x + j);
-#pragma unroll 4
-      for (int j = 0; j < 32; ++j) image_store1(mb_g, mbm, c0 + j, t, x[j]);
       tmem_ld32(S3, c0, x);
-#pragma unroll
-      for (int j = 0; j < 32; j += 8) st8f(bc_g + t * kD + c0 + j, x + j);
+      st32_f(bc_g + t * kD + c0, x);
     }
   }
 
@@ -425,7 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_out_kernel(const OpParams p, 
   float* vn_g = reinterpret_cast<float*>(p.res + p.rl.vnew) + (size_t)ch * mat;
   float* o_g = o_out + off;
   const Mode md = mode_from_enum(p.dot_mode);
-  const float clip = p.clip;
+  const float clip = p.clip, scale = p.scale;
 
   if (warp == 0) {
     tmem_alloc(tslot, 256);
@@ -446,86 +312,39 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_out_kernel(const OpParams p, 
   const uint32_t tb = *tslot;
   const uint32_t S0 = tb, S1 = tb + 128;
   MmaBar mbar{bar, 0u, p.status};
-  const float* gct = gcs + t * kGcPitch;
-  const int KS = kslice(md);
-  const bool lo = md.passes == 3;
 
-  // S0 = wp h_pre,  S1 = (scale qg) h_pre
-  for (int s = 0; s < kD / KS; ++s) {
-    const int k0 = s * KS;
-    const Tile A1[2] = {pool_k(pool, 0), pool_k(pool, 1)};
-    const Tile A2[2] = {pool_k(pool, 2), pool_k(pool, 3)};
-    const Tile Bt[2] = {pool_mn(pool, 4, md), pool_mn(pool, 5, md)};
-    for (int i = 0; i < KS; i += 8) {
-      const int d0 = k0 + i;
-      float x[8], qv[8];
-      ld8f(wp_g + t * kD + d0, x);
-      stage_krow(A1[0], A1[1], lo, md.fmt, t, i, x, 8);
-      ld8(q + t * kD + d0, qv);
+  auto src_wp = [&](int r, int c0, float* x) { ld32_f(wp_g + r * kD + c0, x); };
+  auto src_qg = [&](int r, int c0, float* x) {  // scale sanitize(q e^min(gc, 0))
+    ld32_in(q + r * kD + c0, x);
+    const float* gr = gcs + r * kGcPitch + c0;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) x[j] = p.scale * sanitize(qv[j] * ex(fminf(gct[d0 + j], 0.f)), clip);
-      stage_krow(A2[0], A2[1], lo, md.fmt, t, i, x, 8);
-    }
-    if (warp * 32 >= k0 && warp * 32 < k0 + KS) {
-      for (int c0 = 0; c0 < kD; c0 += 8) {
-        float x[8];
-        ld8f(h_g + t * kD + c0, x);
-        stage_mnrow(Bt[0], Bt[1], lo, md.fmt, t - k0, c0, x, 8);
-      }
-    }
-    staged_sync();
-    if (t == 0) {
-      tc_fence_after();
-      issue_slice(md, S0, A1, Bt, 128, false, s > 0);
-      issue_slice(md, S1, A2, Bt, 128, false, s > 0);
-    }
-    mbar.commit_wait();
-  }
+    for (int j = 0; j < 32; ++j) x[j] = scale * sanitize(x[j] * ex(fminf(gr[j], 0.f)), clip);
+  };
+  auto src_h = [&](int r, int c0, float* x) { ld32_f(h_g + r * kD + c0, x); };
+  auto src_aqk = [&](int r, int c0, float* x) { ld32_f(aqk_g + r * kT + c0, x); };
+  auto tm0 = [&](int, int c0, float* x) { tmem_ld32(S0, (uint32_t)c0, x); };
+
+  // S0 = wp h_pre,  S1 = (scale qg) h_pre   (shared B = h_pre)
+  gemm2(md, pool, mbar, S0, kmaj(src_wp), mn_any(src_h), false, false, S1, kmaj(src_qg), mn_any(NoSrc()), false,
+        false, false, true);
   // v_new = u - S0 (kept in S0 and written as a residual)
   for (int c0 = 0; c0 < kD; c0 += 32) {
-    float x[32], uv[8];
+    float x[32], uv[32];
     tmem_ld32(S0, c0, x);
+    ld32_f(u_g + t * kD + c0, uv);
 #pragma unroll
-    for (int j = 0; j < 32; j += 8) {
-      ld8f(u_g + t * kD + c0 + j, uv);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) x[j + i] = uv[i] - x[j + i];
-      st8f(vn_g + t * kD + c0 + j, x + j);
-    }
+    for (int j = 0; j < 32; ++j) x[j] = uv[j] - x[j];
+    st32_f(vn_g + t * kD + c0, x);
     tmem_st32(S0, c0, x);
   }
   // S1 += Aqk v_new
-  for (int s = 0; s < kT / KS; ++s) {
-    const int k0 = s * KS;
-    const Tile At[2] = {pool_k(pool, 0), pool_k(pool, 1)};
-    const Tile Bt[2] = {pool_mn(pool, 4, md), pool_mn(pool, 5, md)};
-    for (int i = 0; i < KS; i += 8) {
-      float x[8];
-      ld8f(aqk_g + t * kT + k0 + i, x);
-      stage_krow(At[0], At[1], lo, md.fmt, t, i, x, 8);
-    }
-    if (warp * 32 >= k0 && warp * 32 < k0 + KS) {
-      for (int c0 = 0; c0 < kD; c0 += 32) {
-        float x[32];
-        tmem_ld32(S0, (uint32_t)c0, x);
-#pragma unroll
-        for (int j = 0; j < 32; j += 8) stage_mnrow(Bt[0], Bt[1], lo, md.fmt, t - k0, c0 + j, x + j, 8);
-      }
-    }
-    staged_sync();
-    if (t == 0) {
-      tc_fence_after();
-      issue_slice(md, S1, At, Bt, 128, false, true);
-    }
-    mbar.commit_wait();
-  }
+  gemm1(md, pool, mbar, S1, kmaj(src_aqk), mn_own(tm0), false, true);
   for (int c0 = 0; c0 < kD; c0 += 32) {
     float x[32];
     tmem_ld32(S1, c0, x);
 #pragma unroll
     for (int j = 0; j < 32; ++j) x[j] = sanitize(x[j], clip);
-#pragma unroll
-    for (int j = 0; j < 32; j += 8) st8f(o_g + t * kD + c0 + j, x + j);
+    st32_f(o_g + t * kD + c0, x);
   }
   tc_fence_before();
   __syncthreads();

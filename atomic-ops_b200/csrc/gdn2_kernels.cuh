@@ -17,13 +17,13 @@ __host__ __device__ inline uint32_t image_bytes(Mode m) { return image_part_byte
 
 // Per-call residual layout (byte offsets from the residual base), all regions 256-byte aligned.
 struct ResLayout {
-  size_t aqk, ainv, wp, u, mf, mb, bc, hs, vnew, total;
-  uint32_t mf_stride, mb_stride;  // bytes per chunk-head of the two state-transition images
+  size_t aqk, ainv, wp, u, mf, bc, hs, vnew, total;
+  uint32_t mf_stride;  // bytes per chunk-head of the forward state-transition image
 };
 
 __host__ __device__ inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-__host__ __device__ inline ResLayout res_layout(int BH, int NC, Mode fwd_scan, Mode bwd_scan) {
+__host__ __device__ inline ResLayout res_layout(int BH, int NC, Mode fwd_scan) {
   ResLayout r{};
   const size_t nch = (size_t)BH * NC;
   const size_t mat = (size_t)kT * kD * 4;  // one 128x128 fp32 matrix
@@ -33,9 +33,7 @@ __host__ __device__ inline ResLayout res_layout(int BH, int NC, Mode fwd_scan, M
   r.wp = o; o = align256(o + nch * mat);
   r.u = o; o = align256(o + nch * mat);
   r.mf_stride = image_bytes(fwd_scan);
-  r.mb_stride = image_bytes(bwd_scan);
   r.mf = o; o = align256(o + nch * r.mf_stride);
-  r.mb = o; o = align256(o + nch * r.mb_stride);
   r.bc = o; o = align256(o + nch * mat);
   r.hs = o; o = align256(o + (size_t)BH * (NC + 1) * mat);  // h entering each chunk, then h_final
   r.vnew = o; o = align256(o + nch * mat);
@@ -45,13 +43,16 @@ __host__ __device__ inline ResLayout res_layout(int BH, int NC, Mode fwd_scan, M
 
 // Backward workspace layout.
 struct WsLayout {
-  size_t dvl, cc, dhs, total;
+  size_t dvl, cc, dhs, mb, total;
+  uint32_t mb_stride;  // bytes per chunk-head of the backward (transposed) transition image
 };
-__host__ __device__ inline WsLayout ws_layout(int BH, int NC) {
+__host__ __device__ inline WsLayout ws_layout(int BH, int NC, Mode bwd_scan) {
   WsLayout w{};
   const size_t nch = (size_t)BH * NC;
   const size_t mat = (size_t)kT * kD * 4;
   size_t o = 0;
+  w.mb_stride = image_bytes(bwd_scan);
+  w.mb = o; o = align256(o + nch * w.mb_stride);
   w.dvl = o; o = align256(o + nch * mat);
   w.cc = o; o = align256(o + nch * mat);
   w.dhs = o; o = align256(o + nch * mat);  // dh entering each chunk from the right
@@ -177,21 +178,31 @@ __device__ __forceinline__ void image_store1(uint8_t* dst, Mode m, int row, int 
 }
 
 // Column-wise inclusive cumsum of the chunk's gate g (T x D) into shared memory
-// gcs[t * kGcPitch + d]; thread d owns channel d.  Also returns the channel's max, min and
-// whether a positive gate was seen.  (pipeline.py:21 / ref.py:14: gc = cumsum(g) per chunk.)
+// gcs[t * kGcPitch + d].  The chunk is first loaded cooperatively with coalesced 16-byte loads
+// (all threads, many loads in flight), then thread d scans channel d in shared memory.
+// Also returns the channel's max, min and whether a positive gate was seen.
+// (pipeline.py:21 / ref.py:14: gc = cumsum(g) per chunk.)
 constexpr int kGcPitch = 132;  // padded row pitch (floats): conflict-free row reads by row owners
 
 template <class TIn>
 __device__ __forceinline__ void chunk_cumsum(const TIn* __restrict__ g, float* gcs, float& mx, float& mn,
                                              bool& pos) {
   const int d = threadIdx.x;
+#pragma unroll 16
+  for (int i = d; i < kT * (kD / 4); i += kThreads) {
+    const int r = i >> 5, c4 = (i & 31) * 4;
+    float v[4];
+    ld4(g + r * kD + c4, v);
+    *reinterpret_cast<float4*>(gcs + r * kGcPitch + c4) = make_float4(v[0], v[1], v[2], v[3]);
+  }
+  __syncthreads();
   float acc = 0.f;
   mx = -3.0e38f;
   mn = 3.0e38f;
   pos = false;
 #pragma unroll 8
   for (int t = 0; t < kT; ++t) {
-    const float x = to_f(g[t * kD + d]);
+    const float x = gcs[t * kGcPitch + d];
     pos |= x > 0.f;
     acc += x;
     gcs[t * kGcPitch + d] = acc;
@@ -199,7 +210,6 @@ __device__ __forceinline__ void chunk_cumsum(const TIn* __restrict__ g, float* g
     mn = fminf(mn, acc);
   }
 }
-
 
 // ---------------------------------------------------------------------------
 // Generic K-loop over one or two operand pairs (all M = N = 128, K = 128).
@@ -210,20 +220,47 @@ __device__ __forceinline__ void chunk_cumsum(const TIn* __restrict__ g, float* g
 // warp(s) whose rows fall in the current K-slice stage.  TMEM-backed sources are warp-collective,
 // which both patterns respect (whole warps call them).
 // ---------------------------------------------------------------------------
+// An operand: how it is laid out for the MMA and who may fetch its rows.
+//   mn  = false: K-major; the source row is the operand's M/N row and every thread stages its own
+//                row (required for TMEM-backed sources, which only the owning lane can read).
+//   mn  = true : MN-major; the source row is the operand's K row.
+//   any = true : any thread may fetch any row (global- or shared-memory-backed sources): an
+//                MN-major slice is then staged by all threads, (row, 32-column group) items.
+//   any = false: only the owning warp may fetch a row (TMEM-backed): the warp(s) whose rows lie in
+//                the slice stage it.
 template <class Src>
-__device__ __forceinline__ void stage_operand(const Tile tt[2], bool mn, Mode m, int k0, int KS, Src src) {
+struct Opnd {
+  bool mn, any;
+  Src src;
+};
+template <class Src>
+__device__ __forceinline__ Opnd<Src> kmaj(Src s) { return Opnd<Src>{false, false, s}; }
+template <class Src>
+__device__ __forceinline__ Opnd<Src> mn_any(Src s) { return Opnd<Src>{true, true, s}; }
+template <class Src>
+__device__ __forceinline__ Opnd<Src> mn_own(Src s) { return Opnd<Src>{true, false, s}; }
+
+template <class Src>
+__device__ __forceinline__ void stage_op(const Tile tt[2], const Opnd<Src>& op, Mode m, int k0, int KS) {
   const int t = threadIdx.x, warp = t >> 5;
   const bool lo = m.passes == 3;
-  if (!mn) {
+  if (!op.mn) {
     for (int i = 0; i < KS; i += 32) {
       float x[32];
-      src(t, k0 + i, x);
+      op.src(t, k0 + i, x);
       stage_krow(tt[0], tt[1], lo, m.fmt, (uint32_t)t, i, x, 32);
+    }
+  } else if (op.any) {
+    for (int it = t; it < KS * 4; it += kThreads) {
+      const int r = it % KS, c0 = (it / KS) * 32;
+      float x[32];
+      op.src(k0 + r, c0, x);
+      stage_mnrow(tt[0], tt[1], lo, m.fmt, (uint32_t)r, c0, x, 32);
     }
   } else if (warp * 32 >= k0 && warp * 32 < k0 + KS) {
     for (int c0 = 0; c0 < 128; c0 += 32) {
       float x[32];
-      src(t, c0, x);
+      op.src(t, c0, x);
       stage_mnrow(tt[0], tt[1], lo, m.fmt, (uint32_t)(t - k0), c0, x, 32);
     }
   }
@@ -233,14 +270,36 @@ struct NoSrc {
   __device__ void operator()(int, int, float*) const {}
 };
 
-// D1 (+)= op(A1) op(B1)  [and D2 (+)= op(A2) op(B2)], sharing the K-slicing of mode m.
-// share_a / share_b reuse pair 1's staged A / B for pair 2.
-template <class SA1, class SB1, class SA2 = NoSrc, class SB2 = NoSrc>
-__device__ __forceinline__ void gemm_pairs(Mode m, uint32_t pool, MmaBar& mb,
-                                           uint32_t d1, bool a1mn, SA1 sa1, bool b1mn, SB1 sb1, bool neg1,
-                                           bool acc1, int npairs = 1, uint32_t d2 = 0, bool a2mn = false,
-                                           SA2 sa2 = SA2(), bool b2mn = false, SB2 sb2 = SB2(), bool neg2 = false,
-                                           bool acc2 = false, bool share_a = false, bool share_b = false) {
+// D (+)= op(A) op(B), all M = N = K = 128, in K-slices of 128 bytes of mode m.
+template <class SA, class SB>
+__device__ __forceinline__ void gemm1(Mode m, uint32_t pool, MmaBar& mb, uint32_t d, const Opnd<SA>& a,
+                                      const Opnd<SB>& b, bool neg, bool acc) {
+  const int KS = kslice(m), ns = 128 / KS;
+  for (int s = 0; s < ns; ++s) {
+    const int k0 = s * KS;
+    Tile A[2], B[2];
+    A[0] = a.mn ? pool_mn(pool, 0, m) : pool_k(pool, 0);
+    A[1] = a.mn ? pool_mn(pool, 1, m) : pool_k(pool, 1);
+    B[0] = b.mn ? pool_mn(pool, 2, m) : pool_k(pool, 2);
+    B[1] = b.mn ? pool_mn(pool, 3, m) : pool_k(pool, 3);
+    stage_op(A, a, m, k0, KS);
+    stage_op(B, b, m, k0, KS);
+    staged_sync();
+    if (threadIdx.x == 0) {
+      tc_fence_after();
+      issue_slice(m, d, A, B, 128, neg, acc || s > 0);
+    }
+    mb.commit_wait();
+  }
+}
+
+// Two products sharing the K-slicing: D1 (+)= A1 B1 and D2 (+)= A2 B2, where pair 2 reuses pair 1's
+// staged A (share_a) or B (share_b) when set.  Tiles: A1 0-1, B1 2-3, then 4-5 (and 6-7).
+template <class SA1, class SB1, class SA2, class SB2>
+__device__ __forceinline__ void gemm2(Mode m, uint32_t pool, MmaBar& mb, uint32_t d1, const Opnd<SA1>& a1,
+                                      const Opnd<SB1>& b1, bool neg1, bool acc1, uint32_t d2,
+                                      const Opnd<SA2>& a2, const Opnd<SB2>& b2, bool neg2, bool acc2,
+                                      bool share_a, bool share_b) {
   const int KS = kslice(m), ns = 128 / KS;
   auto tiles = [&](int i, bool mn, Tile out[2]) {
     out[0] = mn ? pool_mn(pool, i, m) : pool_k(pool, i);
@@ -249,20 +308,18 @@ __device__ __forceinline__ void gemm_pairs(Mode m, uint32_t pool, MmaBar& mb,
   for (int s = 0; s < ns; ++s) {
     const int k0 = s * KS;
     Tile A1[2], B1[2], A2[2], B2[2];
-    int nt = 0;
-    tiles(nt, a1mn, A1); nt += 2;
-    tiles(nt, b1mn, B1); nt += 2;
-    stage_operand(A1, a1mn, m, k0, KS, sa1);
-    stage_operand(B1, b1mn, m, k0, KS, sb1);
-    if (npairs == 2) {
-      if (share_a) { A2[0] = A1[0]; A2[1] = A1[1]; } else { tiles(nt, a2mn, A2); nt += 2; stage_operand(A2, a2mn, m, k0, KS, sa2); }
-      if (share_b) { B2[0] = B1[0]; B2[1] = B1[1]; } else { tiles(nt, b2mn, B2); nt += 2; stage_operand(B2, b2mn, m, k0, KS, sb2); }
-    }
+    tiles(0, a1.mn, A1);
+    tiles(2, b1.mn, B1);
+    int nt = 4;
+    stage_op(A1, a1, m, k0, KS);
+    stage_op(B1, b1, m, k0, KS);
+    if (share_a) { A2[0] = A1[0]; A2[1] = A1[1]; } else { tiles(nt, a2.mn, A2); nt += 2; stage_op(A2, a2, m, k0, KS); }
+    if (share_b) { B2[0] = B1[0]; B2[1] = B1[1]; } else { tiles(nt, b2.mn, B2); nt += 2; stage_op(B2, b2, m, k0, KS); }
     staged_sync();
     if (threadIdx.x == 0) {
       tc_fence_after();
       issue_slice(m, d1, A1, B1, 128, neg1, acc1 || s > 0);
-      if (npairs == 2) issue_slice(m, d2, A2, B2, 128, neg2, acc2 || s > 0);
+      issue_slice(m, d2, A2, B2, 128, neg2, acc2 || s > 0);
     }
     mb.commit_wait();
   }

@@ -76,10 +76,11 @@ def test_residual_sizes_and_validation():
     lib = _lib.load()
     ok = lib.gdn2_residual_bytes(ctypes.byref(_desc()))
     assert ok > 0 and ok % 256 == 0
-    assert lib.gdn2_bwd_workspace_bytes(ctypes.byref(_desc())) == 3 * 2 * 2 * 128 * 128 * 4
+    # dvl, Cc, dh states (fp32) + the transposed transition image (bf16x3: 64 KB per chunk-head)
+    assert lib.gdn2_bwd_workspace_bytes(ctypes.byref(_desc())) == 3 * 2 * 2 * 128 * 128 * 4 + 2 * 2 * 65536
     # fp32 residual scales with the number of chunk-heads
     big = lib.gdn2_residual_bytes(ctypes.byref(_desc(B=4, H=6, L=2048)))
-    assert 200e6 < big < 300e6
+    assert 180e6 < big < 300e6
     for bad in (dict(L=200), dict(dot=7), dict(dtype=5), dict(wy_eps=1.5), dict(stride_h=100)):
         assert lib.gdn2_residual_bytes(ctypes.byref(_desc(**bad))) == 0, bad
 
