@@ -25,7 +25,7 @@
 namespace gdn2 {
 
 constexpr uint32_t kPreSmem = 1024 + 6 * 16384 + kT * kGcPitch * 4 + 64;
-constexpr uint32_t kBwdSmem = 1024 + 8 * 16384 + kT * kGcPitch * 4 + 3 * kD * 4 + 64;
+constexpr uint32_t kBwdSmem = 1024 + 8 * 16384 + kT * kGcPitch * 4 + 4 * kD * 4 + 64;
 
 __device__ __forceinline__ uint8_t* align1024b(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
@@ -36,7 +36,7 @@ __device__ __forceinline__ uint8_t* align1024b(uint8_t* p) {
 // image M^T = diag(e^gl) - wp^T kg of the reverse scan      (b3_dot_mode, mega.py:31-34)
 // ---------------------------------------------------------------------------------------
 template <class TIn>
-__global__ void __launch_bounds__(kThreads, 1) bwd_pre_kernel(const BwdParams P) {
+__global__ void __launch_bounds__(kCT, 1) bwd_pre_kernel(const BwdParams P) {
   extern __shared__ uint8_t smem_raw[];
   const OpParams& p = P.op;
   uint8_t* sm = align1024b(smem_raw);
@@ -45,7 +45,8 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_pre_kernel(const BwdParams P)
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + 6 * 16384 + kT * kGcPitch * 4);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 1);
 
-  const int t = threadIdx.x, warp = t >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int t = crow(), cb = chalf() * 64;
   const int ch = blockIdx.x, bh = ch / p.NC, c = ch % p.NC;
   const long long off = chunk_off(p, bh, c);
   const TIn* q = reinterpret_cast<const TIn*>(p.q) + off;
@@ -65,7 +66,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_pre_kernel(const BwdParams P)
     tmem_alloc(tslot, 256);
     tmem_relinquish();
   }
-  if (t == 0) {
+  if (tid == 0) {
     mbar_init(bar, 1);
     fence_mbar_init();
   }
@@ -81,50 +82,50 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_pre_kernel(const BwdParams P)
   const uint32_t S0 = tb, S1 = tb + 128;
   MmaBar mb{bar, 0u, p.status};
 
-  auto src_aqk = [&](int r, int c0, float* x) { ld32_f(aqk_g + r * kT + c0, x); };
-  auto src_do = [&](int r, int c0, float* x) { ld32_f(do_ + r * kD + c0, x); };
+  auto src_aqk = [&](int r, int c0, float* x) { ld16_f(aqk_g + r * kT + c0, x); };
+  auto src_do = [&](int r, int c0, float* x) { ld16_f(do_ + r * kD + c0, x); };
   auto src_qg = [&](int r, int c0, float* x) {
-    ld32_in(q + r * kD + c0, x);
+    ld16_in(q + r * kD + c0, x);
     const float* gr = gcs + r * kGcPitch + c0;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) x[j] = scale * sanitize(x[j] * ex(fminf(gr[j], 0.f)), clip);
+    for (int j = 0; j < 16; ++j) x[j] = scale * sanitize(x[j] * ex(fminf(gr[j], 0.f)), clip);
   };
   auto src_kg = [&](int r, int c0, float* x) {  // sanitize(k e^min(gl - gc, 0))
-    ld32_in(k + r * kD + c0, x);
+    ld16_in(k + r * kD + c0, x);
     const float* gr = gcs + r * kGcPitch + c0;
     const float* gl = gcs + (kT - 1) * kGcPitch + c0;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) x[j] = sanitize(x[j] * ex(fminf(gl[j] - gr[j], 0.f)), clip);
+    for (int j = 0; j < 16; ++j) x[j] = sanitize(x[j] * ex(fminf(gl[j] - gr[j], 0.f)), clip);
   };
-  auto src_wp = [&](int r, int c0, float* x) { ld32_f(wp_g + r * kD + c0, x); };
-  auto tm0 = [&](int, int c0, float* x) { tmem_ld32(S0, (uint32_t)c0, x); };
+  auto src_wp = [&](int r, int c0, float* x) { ld16_f(wp_g + r * kD + c0, x); };
+  auto tm0 = [&](int, int c0, float* x) { tmem_ld16(S0, (uint32_t)c0, x); };
 
   // S0 = Aqk^T do, S1 = (scale qg)^T do   (shared B = do)
   gemm2(m3, pool, mb, S0, mn_any(src_aqk), mn_any(src_do), false, false, S1, mn_any(src_qg), mn_any(NoSrc()), false,
         false, false, true);
-  for (int c0 = 0; c0 < kD; c0 += 32) {
-    float x[32];
-    tmem_ld32(S0, c0, x);
-    st32_f(dvl_g + t * kD + c0, x);
+  for (int c0 = cb; c0 < cb + 64; c0 += 16) {
+    float x[16];
+    tmem_ld16(S0, c0, x);
+    st16_f(dvl_g + t * kD + c0, x);
   }
   // S1 -= wp^T dvl
   gemm1(m3, pool, mb, S1, mn_any(src_wp), mn_own(tm0), true, true);
-  for (int c0 = 0; c0 < kD; c0 += 32) {
-    float x[32];
-    tmem_ld32(S1, c0, x);
-    st32_f(cc_g + t * kD + c0, x);
+  for (int c0 = cb; c0 < cb + 64; c0 += 16) {
+    float x[16];
+    tmem_ld16(S1, c0, x);
+    st16_f(cc_g + t * kD + c0, x);
   }
   // transposed transition of this chunk for the reverse scan: M^T = diag(e^gl) - wp^T kg
   gemm1(m3, pool, mb, S0, mn_any(src_wp), mn_any(src_kg), false, false);
   {
     const float dec = ex(fminf(gcs[(kT - 1) * kGcPitch + t], 0.f));
-    for (int c0 = 0; c0 < kD; c0 += 32) {
-      float x[32];
-      tmem_ld32(S0, c0, x);
+    for (int c0 = cb; c0 < cb + 64; c0 += 16) {
+      float x[16];
+      tmem_ld16(S0, c0, x);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) x[j] = ((c0 + j) == t ? dec : 0.f) - x[j];
-#pragma unroll
-      for (int j = 0; j < 32; j += 8) image_store8(mb_g, m3, t, c0 + j, x + j);
+      for (int j = 0; j < 16; ++j) x[j] = ((c0 + j) == t ? dec : 0.f) - x[j];
+      image_store8(mb_g, m3, t, c0, x);
+      image_store8(mb_g, m3, t, c0 + 8, x + 8);
     }
   }
   tc_fence_before();
@@ -136,7 +137,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_pre_kernel(const BwdParams P)
 // bwd_intra
 // ---------------------------------------------------------------------------------------
 template <class TIn>
-__global__ void __launch_bounds__(kThreads, 1) bwd_intra_kernel(const BwdParams P) {
+__global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
   extern __shared__ uint8_t smem_raw[];
   const OpParams& p = P.op;
   uint8_t* sm = align1024b(smem_raw);
@@ -144,11 +145,12 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_intra_kernel(const BwdParams 
   float* gcs = reinterpret_cast<float*>(sm + 8 * 16384);
   float* mid_s = gcs + kT * kGcPitch;
   float* gl_s = mid_s + kD;
-  float* extra_s = gl_s + kD;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(extra_s + kD);
+  float* extra_s = gl_s + kD;  // two halves of the last-row decay term
+  uint64_t* bar = reinterpret_cast<uint64_t*>(extra_s + 2 * kD);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 1);
 
-  const int t = threadIdx.x, warp = t >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int t = crow(), half = chalf(), cb = half * 64;
   const int ch = blockIdx.x, bh = ch / p.NC, c = ch % p.NC;
   const long long off = chunk_off(p, bh, c);
   const TIn* q = reinterpret_cast<const TIn*>(p.q) + off;
@@ -179,7 +181,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_intra_kernel(const BwdParams 
     tmem_alloc(tslot, 512);
     tmem_relinquish();
   }
-  if (t == 0) {
+  if (tid == 0) {
     mbar_init(bar, 1);
     fence_mbar_init();
   }
@@ -187,234 +189,244 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_intra_kernel(const BwdParams 
     float mx, mn;
     bool pos;
     chunk_cumsum(g, gcs, mx, mn, pos);
-    mid_s[t] = 0.5f * (mx + mn);
+    if (tid < kD) mid_s[tid] = 0.5f * (mx + mn);
+  }
+  {
+    // last-row decay term: sum_v dh_next[d, v] h_next[d, v] for channel d = t (two column halves)
+    float acc = 0.f;
+    for (int c0 = cb; c0 < cb + 64; c0 += 16) {
+      float a[16], h[16];
+      ld16_f(dhn_g + t * kD + c0, a);
+      ld16_f(hnext_g + t * kD + c0, h);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) acc = fmaf(a[j], h[j], acc);
+    }
+    extra_s[half * kD + t] = acc;
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  gl_s[t] = gcs[(kT - 1) * kGcPitch + t];
-  {
-    // last-row decay term: sum_v dh_next[d, v] h_next[d, v] for channel d = t
-    float acc = 0.f;
-    for (int c0 = 0; c0 < kD; c0 += 32) {
-      float a[32], h[32];
-      ld32_f(dhn_g + t * kD + c0, a);
-      ld32_f(hnext_g + t * kD + c0, h);
-#pragma unroll
-      for (int j = 0; j < 32; ++j) acc = fmaf(a[j], h[j], acc);
-    }
-    extra_s[t] = acc;
-  }
+  if (tid < kD) gl_s[tid] = gcs[(kT - 1) * kGcPitch + tid];
   __syncthreads();
   const uint32_t tb = *tslot;
   const uint32_t S0 = tb, S1 = tb + 128, S2 = tb + 256, S3 = tb + 384;
   MmaBar mb{bar, 0u, p.status};
+  auto sync_all = [&]() {
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+  };
 
-  // ---- row sources (row r is always the calling thread's own row) ----
+  // ---- row sources: 16 values of row r from column c0 ----
   auto gcrow = [&](int r) { return gcs + r * kGcPitch; };
   auto src_kg = [&](int r, int c0, float* x) {
-    ld32_in(k + r * kD + c0, x);
+    ld16_in(k + r * kD + c0, x);
     const float* gr = gcrow(r) + c0;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) x[j] = sanitize(x[j] * ex(fminf(gl_s[c0 + j] - gr[j], 0.f)), clip);
+    for (int j = 0; j < 16; ++j) x[j] = sanitize(x[j] * ex(fminf(gl_s[c0 + j] - gr[j], 0.f)), clip);
   };
-  auto src_dhn = [&](int r, int c0, float* x) { ld32_f(dhn_g + r * kD + c0, x); };
+  auto src_dhn = [&](int r, int c0, float* x) { ld16_f(dhn_g + r * kD + c0, x); };
   auto src_hpre_em = [&](int r, int c0, float* x) {  // row d = r of e^m h_pre
-    ld32_f(hpre_g + r * kD + c0, x);
+    ld16_f(hpre_g + r * kD + c0, x);
     const float s = ex(mid_s[r]);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) x[j] *= s;
+    for (int j = 0; j < 16; ++j) x[j] *= s;
   };
   auto src_dhn_gl = [&](int r, int c0, float* x) {  // row d = r of e^(gl-m) dh_next
-    ld32_f(dhn_g + r * kD + c0, x);
+    ld16_f(dhn_g + r * kD + c0, x);
     const float s = ex(gl_s[r] - mid_s[r]);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) x[j] *= s;
+    for (int j = 0; j < 16; ++j) x[j] *= s;
   };
   auto src_bkE = [&](int r, int c0, float* x) {
-    float kv[32];
-    ld32_in(b + r * kD + c0, x);
-    ld32_in(k + r * kD + c0, kv);
+    float kv[16];
+    ld16_in(b + r * kD + c0, x);
+    ld16_in(k + r * kD + c0, kv);
     const float* gr = gcrow(r) + c0;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) x[j] = x[j] * kv[j] * ex(gr[j] - mid_s[c0 + j]);
+    for (int j = 0; j < 16; ++j) x[j] = x[j] * kv[j] * ex(gr[j] - mid_s[c0 + j]);
   };
   auto src_qE = [&](int r, int c0, float* x) {
-    ld32_in(q + r * kD + c0, x);
+    ld16_in(q + r * kD + c0, x);
     const float* gr = gcrow(r) + c0;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) x[j] = scale * x[j] * ex(gr[j] - mid_s[c0 + j]);
+    for (int j = 0; j < 16; ++j) x[j] = scale * x[j] * ex(gr[j] - mid_s[c0 + j]);
   };
   auto src_kF = [&](int r, int c0, float* x) {
-    ld32_in(k + r * kD + c0, x);
+    ld16_in(k + r * kD + c0, x);
     const float* gr = gcrow(r) + c0;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) x[j] = x[j] * ex(mid_s[c0 + j] - gr[j]);
+    for (int j = 0; j < 16; ++j) x[j] = x[j] * ex(mid_s[c0 + j] - gr[j]);
   };
   auto src_wv = [&](int r, int c0, float* x) {
-    float vv[32];
-    ld32_in(w + r * kD + c0, x);
-    ld32_in(v + r * kD + c0, vv);
+    float vv[16];
+    ld16_in(w + r * kD + c0, x);
+    ld16_in(v + r * kD + c0, vv);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) x[j] *= vv[j];
+    for (int j = 0; j < 16; ++j) x[j] *= vv[j];
   };
-  auto src_ainv = [&](int r, int c0, float* x) { ld32_f(ainv_g + r * kT + c0, x); };
-  auto src_vnew = [&](int r, int c0, float* x) { ld32_f(vnew_g + r * kD + c0, x); };
-  auto src_do = [&](int r, int c0, float* x) { ld32_f(do_ + r * kD + c0, x); };
+  auto src_ainv = [&](int r, int c0, float* x) { ld16_f(ainv_g + r * kT + c0, x); };
+  auto src_vnew = [&](int r, int c0, float* x) { ld16_f(vnew_g + r * kD + c0, x); };
+  auto src_do = [&](int r, int c0, float* x) { ld16_f(do_ + r * kD + c0, x); };
   auto src_do_s = [&](int r, int c0, float* x) {
-    ld32_f(do_ + r * kD + c0, x);
+    ld16_f(do_ + r * kD + c0, x);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) x[j] *= scale;
+    for (int j = 0; j < 16; ++j) x[j] *= scale;
   };
-  auto tm = [&](uint32_t slot) { return [=](int, int c0, float* x) { tmem_ld32(slot, (uint32_t)c0, x); }; };
+  auto tm = [&](uint32_t slot) { return [=](int, int c0, float* x) { tmem_ld16(slot, (uint32_t)c0, x); }; };
   auto tm_scaled = [&](uint32_t slot) {
     return [=](int, int c0, float* x) {
-      tmem_ld32(slot, (uint32_t)c0, x);
+      tmem_ld16(slot, (uint32_t)c0, x);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) x[j] *= scale;
+      for (int j = 0; j < 16; ++j) x[j] *= scale;
     };
   };
 
   // 1. S0 = dv_new = sanitize(dvl + kg dh_next)                                  [B1, b3 mode]
   gemm1(m3, pool, mb, S0, kmaj(src_kg), mn_any(src_dhn), false, false);
-  for (int c0 = 0; c0 < kD; c0 += 32) {
-    float x[32], y[32];
-    tmem_ld32(S0, c0, x);
-    ld32_f(dvl_g + t * kD + c0, y);
+  for (int c0 = cb; c0 < cb + 64; c0 += 16) {
+    float x[16], y[16];
+    tmem_ld16(S0, c0, x);
+    ld16_f(dvl_g + t * kD + c0, y);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) x[j] = sanitize(x[j] + y[j], clip);
-    tmem_st32(S0, c0, x);
+    for (int j = 0; j < 16; ++j) x[j] = sanitize(x[j] + y[j], clip);
+    tmem_st16(S0, c0, x);
   }
+  sync_all();
   // 2. S1 = dwp' = -dv_new (e^m h_pre)^T                                          [B3]
   gemm1(m3, pool, mb, S1, kmaj(tm(S0)), kmaj(src_hpre_em), true, false);
   // 3. S2 = dA = sanitize(dwp' (bk E)^T + dv_new (w v)^T)                          [B3]
   gemm2(m3, pool, mb, S2, kmaj(tm(S1)), kmaj(src_bkE), false, false, S2, kmaj(tm(S0)), kmaj(src_wv), false, true,
         false, false);
-  for (int c0 = 0; c0 < kT; c0 += 32) {
-    float x[32];
-    tmem_ld32(S2, c0, x);
+  for (int c0 = cb; c0 < cb + 64; c0 += 16) {
+    float x[16];
+    tmem_ld16(S2, c0, x);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) x[j] = sanitize(x[j], clip);
-    tmem_st32(S2, c0, x);
+    for (int j = 0; j < 16; ++j) x[j] = sanitize(x[j], clip);
+    tmem_st16(S2, c0, x);
   }
+  sync_all();
   // 4. S3 = dwv = A^T dv_new;  dw = dwv v, dv = dwv w                              [B3]
   gemm1(m3, pool, mb, S3, mn_any(src_ainv), mn_own(tm(S0)), false, false);
-  for (int c0 = 0; c0 < kD; c0 += 32) {
-    float x[32], a[32], y[32];
-    tmem_ld32(S3, c0, x);
-    ld32_in(v + t * kD + c0, a);
+  for (int c0 = cb; c0 < cb + 64; c0 += 16) {
+    float x[16], a[16], y[16];
+    tmem_ld16(S3, c0, x);
+    ld16_in(v + t * kD + c0, a);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) y[j] = sanitize(x[j] * a[j], clip);
-    st32_out(dw + t * kD + c0, y);
-    ld32_in(w + t * kD + c0, a);
+    for (int j = 0; j < 16; ++j) y[j] = sanitize(x[j] * a[j], clip);
+    st16_out(dw + t * kD + c0, y);
+    ld16_in(w + t * kD + c0, a);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) y[j] = sanitize(x[j] * a[j], clip);
-    st32_out(dv + t * kD + c0, y);
+    for (int j = 0; j < 16; ++j) y[j] = sanitize(x[j] * a[j], clip);
+    st16_out(dv + t * kD + c0, y);
   }
   // 5. S0 = tmp = sanitize(dA A^T)                                                   [B3]
   gemm1(m3, pool, mb, S0, kmaj(tm(S2)), kmaj(src_ainv), false, false);
-  for (int c0 = 0; c0 < kT; c0 += 32) {
-    float x[32];
-    tmem_ld32(S0, c0, x);
+  for (int c0 = cb; c0 < cb + 64; c0 += 16) {
+    float x[16];
+    tmem_ld16(S0, c0, x);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) x[j] = sanitize(x[j], clip);
-    tmem_st32(S0, c0, x);
+    for (int j = 0; j < 16; ++j) x[j] = sanitize(x[j], clip);
+    tmem_st16(S0, c0, x);
   }
+  sync_all();
   // 6. S2 = dAkk = sanitize(-(1-eps) A^T tmp) strict                                  [B3]
   gemm1(m3, pool, mb, S2, mn_any(src_ainv), mn_own(tm(S0)), true, false);
   {
     const float keep = 1.0f - p.eps;
-    for (int c0 = 0; c0 < kT; c0 += 32) {
-      float x[32];
-      tmem_ld32(S2, c0, x);
+    for (int c0 = cb; c0 < cb + 64; c0 += 16) {
+      float x[16];
+      tmem_ld16(S2, c0, x);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) x[j] = (c0 + j < t) ? sanitize(x[j] * keep, clip) : 0.f;
-      tmem_st32(S2, c0, x);
+      for (int j = 0; j < 16; ++j) x[j] = (c0 + j < t) ? sanitize(x[j] * keep, clip) : 0.f;
+      tmem_st16(S2, c0, x);
     }
   }
+  sync_all();
   // 7. S0 = A^T dwp' (B3)  +  dAkk (k F) (B4, highest)
   gemm1(m3, pool, mb, S0, mn_any(src_ainv), mn_own(tm(S1)), false, false);
   gemm1(mh, pool, mb, S0, kmaj(tm(S2)), mn_any(src_kF), false, true);
   // 8. S1 = dAqk = (do v_new^T) causal                                              [B2]
   gemm1(m3, pool, mb, S1, kmaj(src_do), kmaj(src_vnew), false, false);
-  for (int c0 = 0; c0 < kT; c0 += 32) {
-    float x[32];
-    tmem_ld32(S1, c0, x);
+  for (int c0 = cb; c0 < cb + 64; c0 += 16) {
+    float x[16];
+    tmem_ld16(S1, c0, x);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) x[j] = (c0 + j <= t) ? x[j] : 0.f;
-    tmem_st32(S1, c0, x);
+    for (int j = 0; j < 16; ++j) x[j] = (c0 + j <= t) ? x[j] : 0.f;
+    tmem_st16(S1, c0, x);
   }
+  sync_all();
   // 9. S3 = scale do (e^m h_pre)^T (B3)  +  scale dAqk (k F) (B4)
   gemm1(m3, pool, mb, S3, kmaj(src_do_s), kmaj(src_hpre_em), false, false);
   gemm1(mh, pool, mb, S3, kmaj(tm_scaled(S1)), mn_any(src_kF), false, true);
   // 10.-11. finish dq and db;  S3 <- dgc partial;  S0 <- Dbk b E (pre-scaled dk partial)
   {
     const float* gr = gcrow(t);
-    for (int c0 = 0; c0 < kD; c0 += 32) {
-      float x[32], y[32], qv[32], kv[32], bv[32], E[32];
+    for (int c0 = cb; c0 < cb + 64; c0 += 16) {
+      float x[16], y[16], qv[16], kv[16], bv[16], E[16], dgcp[16];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) E[j] = ex(gr[c0 + j] - mid_s[c0 + j]);
-      ld32_in(q + t * kD + c0, qv);
-      ld32_in(k + t * kD + c0, kv);
-      ld32_in(b + t * kD + c0, bv);
-      tmem_ld32(S3, c0, x);  // Dq / E
+      for (int j = 0; j < 16; ++j) E[j] = ex(gr[c0 + j] - mid_s[c0 + j]);
+      ld16_in(q + t * kD + c0, qv);
+      ld16_in(k + t * kD + c0, kv);
+      ld16_in(b + t * kD + c0, bv);
+      tmem_ld16(S3, c0, x);  // Dq / E
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
+      for (int j = 0; j < 16; ++j) {
         x[j] *= E[j];
         y[j] = sanitize(x[j], clip);
+        dgcp[j] = qv[j] * x[j];
       }
-      st32_out(dq + t * kD + c0, y);
-      float dgcp[32];
+      st16_out(dq + t * kD + c0, y);
+      tmem_ld16(S0, c0, x);  // Dbk / E
 #pragma unroll
-      for (int j = 0; j < 32; ++j) dgcp[j] = qv[j] * x[j];
-      tmem_ld32(S0, c0, x);  // Dbk / E
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
+      for (int j = 0; j < 16; ++j) {
         x[j] *= E[j];
         y[j] = sanitize(x[j] * kv[j], clip);
         dgcp[j] += 2.f * bv[j] * kv[j] * x[j];
         x[j] = x[j] * bv[j] * E[j];
       }
-      st32_out(db + t * kD + c0, y);
-      tmem_st32(S3, c0, dgcp);
-      tmem_st32(S0, c0, x);
+      st16_out(db + t * kD + c0, y);
+      tmem_st16(S3, c0, dgcp);
+      tmem_st16(S0, c0, x);
     }
   }
+  sync_all();
   // 12. S0 += v_new (e^(gl-m) dh_next)^T (B3)  +  scale dAqk^T (q E) + dAkk^T (bk E) (B4)
   gemm1(m3, pool, mb, S0, kmaj(src_vnew), kmaj(src_dhn_gl), false, true);
   gemm2(mh, pool, mb, S0, mn_own(tm(S1)), mn_any(src_qE), false, true, S0, mn_own(tm(S2)), mn_any(src_bkE), false,
         true, false, false);
-  // 13. dk = F o S0;  dgc = S3 - k o dk (+ decay term on the last row);  dgc -> smem (gcs rows)
+  // 13. dk = F o S0;  dgc = S3 - k o dk (+ decay term on the last row).  dgc overwrites this
+  //     thread's own half-row of gcs (no other thread reads that row any more).
   {
     float* gr = gcs + t * kGcPitch;
-    for (int c0 = 0; c0 < kD; c0 += 32) {
-      float x[32], y[32], kv[32], dgcp[32];
-      ld32_in(k + t * kD + c0, kv);
-      tmem_ld32(S0, c0, x);
-      tmem_ld32(S3, c0, dgcp);
+    for (int c0 = cb; c0 < cb + 64; c0 += 16) {
+      float x[16], y[16], kv[16], dgcp[16];
+      ld16_in(k + t * kD + c0, kv);
+      tmem_ld16(S0, c0, x);
+      tmem_ld16(S3, c0, dgcp);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
+      for (int j = 0; j < 16; ++j) {
         x[j] *= ex(mid_s[c0 + j] - gr[c0 + j]);
         y[j] = sanitize(x[j], clip);
         dgcp[j] -= kv[j] * x[j];
-        if (t == kT - 1) dgcp[j] += extra_s[c0 + j];
+        if (t == kT - 1) dgcp[j] += extra_s[c0 + j] + extra_s[kD + c0 + j];
       }
-      st32_out(dk + t * kD + c0, y);
+      st16_out(dk + t * kD + c0, y);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) gr[c0 + j] = dgcp[j];
+      for (int j = 0; j < 16; ++j) gr[c0 + j] = dgcp[j];
     }
   }
   __syncthreads();
   // 14. dg = reverse cumsum of dgc over the chunk (B5)
-  {
+  if (tid < kD) {
     float acc = 0.f;
     for (int r = kT - 1; r >= 0; --r) {
-      acc += gcs[r * kGcPitch + t];
+      acc += gcs[r * kGcPitch + tid];
       const float val = sanitize(acc, clip);
       if constexpr (sizeof(TIn) == 4) {
-        dg[r * kD + t] = val;
+        dg[r * kD + tid] = val;
       } else {
-        dg[r * kD + t] = __float2bfloat16_rn(val);
+        dg[r * kD + tid] = __float2bfloat16_rn(val);
       }
     }
   }
@@ -427,7 +439,7 @@ template <class TIn>
 static cudaError_t launch_bwd_pre_t(const BwdParams& p, int nblocks, cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(bwd_pre_kernel<TIn>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPreSmem);
   if (e != cudaSuccess) return e;
-  bwd_pre_kernel<TIn><<<nblocks, kThreads, kPreSmem, st>>>(p);
+  bwd_pre_kernel<TIn><<<nblocks, kCT, kPreSmem, st>>>(p);
   return cudaGetLastError();
 }
 template <class TIn>
@@ -435,7 +447,7 @@ static cudaError_t launch_bwd_intra_t(const BwdParams& p, int nblocks, cudaStrea
   cudaError_t e =
       cudaFuncSetAttribute(bwd_intra_kernel<TIn>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBwdSmem);
   if (e != cudaSuccess) return e;
-  bwd_intra_kernel<TIn><<<nblocks, kThreads, kBwdSmem, st>>>(p);
+  bwd_intra_kernel<TIn><<<nblocks, kCT, kBwdSmem, st>>>(p);
   return cudaGetLastError();
 }
 

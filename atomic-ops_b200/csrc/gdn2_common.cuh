@@ -211,6 +211,36 @@ __device__ __forceinline__ void tmem_ld32(uint32_t tbase, uint32_t col, float v[
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Load 16 consecutive fp32 columns of this thread's lane (row) starting at column col.
+__device__ __forceinline__ void tmem_ld16(uint32_t tbase, uint32_t col, float v[16]) {
+  uint32_t r[16];
+  const uint32_t a = tmem_lane_base(tbase) + col;
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(a));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Store 16 consecutive fp32 columns into this thread's lane.
+__device__ __forceinline__ void tmem_st16(uint32_t tbase, uint32_t col, const float v[16]) {
+  uint32_t r[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(v[i]);
+  const uint32_t a = tmem_lane_base(tbase) + col;
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(a),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 // Store 32 consecutive fp32 columns into this thread's lane.
 __device__ __forceinline__ void tmem_st32(uint32_t tbase, uint32_t col, const float v[32]) {
   uint32_t r[32];
@@ -363,23 +393,18 @@ __device__ __forceinline__ void mma_tiles(int fmt, int passes, uint32_t d_tmem, 
 // K-major piece: 4 consecutive k (tf32) or 8 consecutive k (bf16) of row mn.
 // MN-major piece: 4 consecutive mn (tf32) or 8 consecutive mn (bf16) of row k.
 // `v` holds 4 (tf32) or 8 (bf16) fp32 values; hi and (if lo_addr != 0) lo parts are written.
-__device__ __forceinline__ void put_piece(uint32_t hi_addr, uint32_t lo_addr, int fmt, const float* v) {
-  if (fmt == kTF32) {
-    uint32_t h[4], l[4];
+// The operand format is a template parameter so that every index into the value arrays is a
+// compile-time constant (the arrays stay in registers).
+template <int FMT>
+__device__ __forceinline__ void put_piece_t(uint32_t hi_addr, uint32_t lo_addr, const float* v) {
+  uint32_t h[4], l[4];
+  if constexpr (FMT == kTF32) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       h[i] = tf32_rna(v[i]);
       l[i] = tf32_rna(v[i] - __uint_as_float(h[i]));
     }
-    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(hi_addr), "r"(h[0]), "r"(h[1]), "r"(h[2]),
-                 "r"(h[3])
-                 : "memory");
-    if (lo_addr)
-      asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(lo_addr), "r"(l[0]), "r"(l[1]), "r"(l[2]),
-                   "r"(l[3])
-                   : "memory");
   } else {
-    uint32_t h[4], l[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       __nv_bfloat162 hv = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
@@ -388,14 +413,13 @@ __device__ __forceinline__ void put_piece(uint32_t hi_addr, uint32_t lo_addr, in
       h[i] = *reinterpret_cast<uint32_t*>(&hv);
       l[i] = *reinterpret_cast<uint32_t*>(&lv);
     }
-    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(hi_addr), "r"(h[0]), "r"(h[1]), "r"(h[2]),
-                 "r"(h[3])
-                 : "memory");
-    if (lo_addr)
-      asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(lo_addr), "r"(l[0]), "r"(l[1]), "r"(l[2]),
-                   "r"(l[3])
-                   : "memory");
   }
+  asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(hi_addr), "r"(h[0]), "r"(h[1]), "r"(h[2]), "r"(h[3])
+               : "memory");
+  if (lo_addr)
+    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(lo_addr), "r"(l[0]), "r"(l[1]), "r"(l[2]),
+                 "r"(l[3])
+                 : "memory");
 }
 
 // Byte offset of piece p (16-byte unit index along K) of row mn in a K-major tile.
@@ -411,25 +435,45 @@ __device__ __forceinline__ uint32_t mnoff(const Tile& t, uint32_t k, uint32_t p)
   return p * 128u + (k >> 3) * t.lbo + (k & 7u) * 16u;
 }
 
-// Stage `nvals` fp32 values of operand row `mn` (K-major), starting at element k0 of the tile's
-// K range, from v[]. nvals must be a multiple of the piece width (4 tf32 / 8 bf16).
-__device__ __forceinline__ void stage_krow(const Tile& hi, const Tile& lo, bool with_lo, int fmt, uint32_t mn,
-                                           int k0, const float* v, int nvals) {
-  const int w = (fmt == kTF32) ? 4 : 8;
-  for (int i = 0; i < nvals; i += w) {
-    const uint32_t p = (uint32_t)((k0 + i) / w);
-    const uint32_t o = koff(mn, p, hi.sbo);
-    put_piece(hi.addr + o, with_lo ? lo.addr + o : 0u, fmt, v + i);
+// Stage N fp32 values (N a multiple of the piece width) of operand row `mn` (K-major), starting at
+// element k0 of the tile's K range.
+template <int FMT, int N>
+__device__ __forceinline__ void stage_krow_t(const Tile& hi, const Tile& lo, bool with_lo, uint32_t mn, int k0,
+                                             const float* v) {
+  constexpr int W = (FMT == kTF32) ? 4 : 8;
+#pragma unroll
+  for (int i = 0; i < N; i += W) {
+    const uint32_t pc = (uint32_t)((k0 + i) / W);
+    const uint32_t o = koff(mn, pc, hi.sbo);
+    put_piece_t<FMT>(hi.addr + o, with_lo ? lo.addr + o : 0u, v + i);
   }
 }
-// Stage `nvals` values of k-row `k` (MN-major), starting at MN element m0.
+// Stage N values of k-row `k` (MN-major), starting at MN element m0.
+template <int FMT, int N>
+__device__ __forceinline__ void stage_mnrow_t(const Tile& hi, const Tile& lo, bool with_lo, uint32_t k, int m0,
+                                              const float* v) {
+  constexpr int W = (FMT == kTF32) ? 4 : 8;
+#pragma unroll
+  for (int i = 0; i < N; i += W) {
+    const uint32_t pc = (uint32_t)((m0 + i) / W);
+    const uint32_t o = mnoff(hi, k, pc);
+    put_piece_t<FMT>(hi.addr + o, with_lo ? lo.addr + o : 0u, v + i);
+  }
+}
+
+// Runtime-format wrappers (the selftest and the scan use them with constant sizes).
+__device__ __forceinline__ void stage_krow(const Tile& hi, const Tile& lo, bool with_lo, int fmt, uint32_t mn,
+                                           int k0, const float* v, int nvals) {
+  for (int i = 0; i < nvals; i += 8) {
+    if (fmt == kTF32) stage_krow_t<kTF32, 8>(hi, lo, with_lo, mn, k0 + i, v + i);
+    else stage_krow_t<kBF16, 8>(hi, lo, with_lo, mn, k0 + i, v + i);
+  }
+}
 __device__ __forceinline__ void stage_mnrow(const Tile& hi, const Tile& lo, bool with_lo, int fmt, uint32_t k,
                                             int m0, const float* v, int nvals) {
-  const int w = (fmt == kTF32) ? 4 : 8;
-  for (int i = 0; i < nvals; i += w) {
-    const uint32_t p = (uint32_t)((m0 + i) / w);
-    const uint32_t o = mnoff(hi, k, p);
-    put_piece(hi.addr + o, with_lo ? lo.addr + o : 0u, fmt, v + i);
+  for (int i = 0; i < nvals; i += 8) {
+    if (fmt == kTF32) stage_mnrow_t<kTF32, 8>(hi, lo, with_lo, k, m0 + i, v + i);
+    else stage_mnrow_t<kBF16, 8>(hi, lo, with_lo, k, m0 + i, v + i);
   }
 }
 

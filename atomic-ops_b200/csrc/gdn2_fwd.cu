@@ -42,7 +42,7 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
 // fwd_intra
 // ---------------------------------------------------------------------------------------
 template <class TIn>
-__global__ void __launch_bounds__(kThreads, 1) fwd_intra_kernel(const OpParams p) {
+__global__ void __launch_bounds__(kCT, 1) fwd_intra_kernel(const OpParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
   const uint32_t pool = smem_u32(sm);
@@ -53,7 +53,9 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_intra_kernel(const OpParams p
   uint64_t* bar = reinterpret_cast<uint64_t*>(gl_s + kD);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 1);
 
-  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int t = crow(), half = chalf();
+  const int cb = half * 64;  // this thread's 64 columns of its row
   const int ch = blockIdx.x, bh = ch / p.NC, c = ch % p.NC;
   const long long off = chunk_off(p, bh, c);
   const TIn* q = reinterpret_cast<const TIn*>(p.q) + off;
@@ -78,7 +80,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_intra_kernel(const OpParams p
     tmem_alloc(tslot, 512);
     tmem_relinquish();
   }
-  if (t == 0) {
+  if (tid == 0) {
     mbar_init(bar, 1);
     fence_mbar_init();
   }
@@ -86,77 +88,80 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_intra_kernel(const OpParams p
     float mx, mn;
     bool pos;
     chunk_cumsum(g, gcs, mx, mn, pos);
-    mid_s[t] = 0.5f * (mx + mn);
-    if (pos) atomicOr(p.status, kStatusPositiveGate);
-    if (mx - mn > kSpanMax) atomicOr(p.status, kStatusSpan);
+    if (tid < kD) {
+      mid_s[tid] = 0.5f * (mx + mn);
+      if (pos) atomicOr(p.status, kStatusPositiveGate);
+      if (mx - mn > kSpanMax) atomicOr(p.status, kStatusSpan);
+    }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  gl_s[t] = gcs[(kT - 1) * kGcPitch + t];
+  if (tid < kD) gl_s[tid] = gcs[(kT - 1) * kGcPitch + tid];
   const uint32_t tb = *tslot;
   const uint32_t S0 = tb, S1 = tb + 128, S2 = tb + 256, S3 = tb + 384;
   MmaBar mbar{bar, 0u, p.status};
+  __syncthreads();
 
-  // ---- row sources (row r; global / shared-memory sources may be called for any row) ----
+  // ---- row sources: 16 values of row r from column c0 (global / smem ones for any row) -------
   auto src_qE = [&](int r, int c0, float* x) {  // q e^(gc - m)
-    ld32_in(q + r * kD + c0, x);
+    ld16_in(q + r * kD + c0, x);
     const float* gr = gcs + r * kGcPitch + c0;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) x[j] *= ex(gr[j] - mid_s[c0 + j]);
+    for (int j = 0; j < 16; ++j) x[j] *= ex(gr[j] - mid_s[c0 + j]);
   };
   auto src_bkE = [&](int r, int c0, float* x) {  // b k e^(gc - m)
-    float kv[32];
-    ld32_in(b + r * kD + c0, x);
-    ld32_in(k + r * kD + c0, kv);
+    float kv[16];
+    ld16_in(b + r * kD + c0, x);
+    ld16_in(k + r * kD + c0, kv);
     const float* gr = gcs + r * kGcPitch + c0;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) x[j] = x[j] * kv[j] * ex(gr[j] - mid_s[c0 + j]);
+    for (int j = 0; j < 16; ++j) x[j] = x[j] * kv[j] * ex(gr[j] - mid_s[c0 + j]);
   };
   auto src_kF = [&](int r, int c0, float* x) {  // k e^(m - gc)
-    ld32_in(k + r * kD + c0, x);
+    ld16_in(k + r * kD + c0, x);
     const float* gr = gcs + r * kGcPitch + c0;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) x[j] *= ex(mid_s[c0 + j] - gr[j]);
+    for (int j = 0; j < 16; ++j) x[j] *= ex(mid_s[c0 + j] - gr[j]);
   };
   auto src_kb = [&](int r, int c0, float* x) {  // b k e^min(gc, 0)
-    float kv[32];
-    ld32_in(b + r * kD + c0, x);
-    ld32_in(k + r * kD + c0, kv);
+    float kv[16];
+    ld16_in(b + r * kD + c0, x);
+    ld16_in(k + r * kD + c0, kv);
     const float* gr = gcs + r * kGcPitch + c0;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) x[j] = x[j] * kv[j] * ex(fminf(gr[j], 0.f));
+    for (int j = 0; j < 16; ++j) x[j] = x[j] * kv[j] * ex(fminf(gr[j], 0.f));
   };
   auto src_wv = [&](int r, int c0, float* x) {
-    float vv[32];
-    ld32_in(w + r * kD + c0, x);
-    ld32_in(v + r * kD + c0, vv);
+    float vv[16];
+    ld16_in(w + r * kD + c0, x);
+    ld16_in(v + r * kD + c0, vv);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) x[j] *= vv[j];
+    for (int j = 0; j < 16; ++j) x[j] *= vv[j];
   };
   auto src_kg = [&](int r, int c0, float* x) {  // sanitize(k e^min(gl - gc, 0))
-    ld32_in(k + r * kD + c0, x);
+    ld16_in(k + r * kD + c0, x);
     const float* gr = gcs + r * kGcPitch + c0;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) x[j] = sanitize(x[j] * ex(fminf(gl_s[c0 + j] - gr[j], 0.f)), clip);
+    for (int j = 0; j < 16; ++j) x[j] = sanitize(x[j] * ex(fminf(gl_s[c0 + j] - gr[j], 0.f)), clip);
   };
   auto src_dinv = [&](int r, int c0, float* x) {  // row r of the block-diagonal Dg^-1
     if ((c0 >> 5) == (r >> 5)) {
-      const float* src = dsm + (r >> 5) * 1056 + (r & 31) * 33;
+      const float* src = dsm + (r >> 5) * 1056 + (r & 31) * 33 + (c0 & 31);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) x[j] = src[j];
+      for (int j = 0; j < 16; ++j) x[j] = src[j];
     } else {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) x[j] = 0.f;
+      for (int j = 0; j < 16; ++j) x[j] = 0.f;
     }
   };
   auto src_R = [&](int r, int c0, float* x) {  // strictly block-lower part of Se (TMEM S1, owner)
-    tmem_ld32(S1, (uint32_t)c0, x);
+    tmem_ld16(S1, (uint32_t)c0, x);
     const int lim = (r >> 5) << 5;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) x[j] = (c0 + j < lim) ? x[j] : 0.f;
+    for (int j = 0; j < 16; ++j) x[j] = (c0 + j < lim) ? x[j] : 0.f;
   };
-  auto tm = [&](uint32_t slot) { return [=](int, int c0, float* x) { tmem_ld32(slot, (uint32_t)c0, x); }; };
+  auto tm = [&](uint32_t slot) { return [=](int, int c0, float* x) { tmem_ld16(slot, (uint32_t)c0, x); }; };
 
   // ---- 1. scores: S0 = (q E)(k F)^T, S1 = (b k E)(k F)^T                      (dot mode) --------
   gemm2(md, pool, mbar, S0, kmaj(src_qE), kmaj(src_kF), false, false, S1, kmaj(src_bkE), kmaj(NoSrc()), false,
@@ -166,19 +171,19 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_intra_kernel(const OpParams p
   {
     const float keep = 1.0f - p.eps;
     const int blk = t >> 5;
-    for (int c0 = 0; c0 < kT; c0 += 32) {
-      float x[32];
-      tmem_ld32(S0, c0, x);
+    for (int c0 = cb; c0 < cb + 64; c0 += 16) {
+      float x[16];
+      tmem_ld16(S0, c0, x);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) x[j] = (c0 + j <= t) ? sanitize(p.scale * x[j], clip) : 0.f;
-      st32_f(aqk_g + t * kT + c0, x);
-      tmem_ld32(S1, c0, x);
+      for (int j = 0; j < 16; ++j) x[j] = (c0 + j <= t) ? sanitize(p.scale * x[j], clip) : 0.f;
+      st16_f(aqk_g + t * kT + c0, x);
+      tmem_ld16(S1, c0, x);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) x[j] = (c0 + j < t) ? keep * sanitize(x[j], clip) : 0.f;
-      tmem_st32(S1, c0, x);
+      for (int j = 0; j < 16; ++j) x[j] = (c0 + j < t) ? keep * sanitize(x[j], clip) : 0.f;
+      tmem_st16(S1, c0, x);
       if ((c0 >> 5) == blk) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) dsm[blk * 1056 + lane * 33 + j] = x[j];
+        for (int j = 0; j < 16; ++j) dsm[blk * 1056 + (t & 31) * 33 + (c0 & 31) + j] = x[j];
       }
     }
   }
@@ -187,7 +192,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_intra_kernel(const OpParams p
   tc_fence_after();
 
   // ---- 3. diagonal-block inverses (forward substitution, warp = block, lane = column) ----------
-  {
+  if (warp < 4) {
     const float* Sb = dsm + warp * 1056;
     float x[32];
 #pragma unroll
@@ -207,57 +212,65 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_intra_kernel(const OpParams p
   gemm1(ms, pool, mbar, S0, kmaj(src_dinv), mn_own(src_R), false, false);   // W -> S0
   gemm1(ms, pool, mbar, S2, kmaj(tm(S0)), mn_own(tm(S0)), false, false);    // W^2 -> S2
   gemm1(ms, pool, mbar, S3, kmaj(tm(S2)), mn_any(src_dinv), false, false);  // W^2 Dg^-1 -> S3
-  for (int c0 = 0; c0 < kT; c0 += 32) {                                      // P = S3 + Dg^-1
-    float x[32], dv[32];
-    tmem_ld32(S3, c0, x);
+  for (int c0 = cb; c0 < cb + 64; c0 += 16) {                               // P = S3 + Dg^-1
+    float x[16], dv[16];
+    tmem_ld16(S3, c0, x);
     src_dinv(t, c0, dv);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) x[j] += dv[j];
-    tmem_st32(S3, c0, x);
+    for (int j = 0; j < 16; ++j) x[j] += dv[j];
+    tmem_st16(S3, c0, x);
   }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
   gemm1(ms, pool, mbar, S2, kmaj(tm(S0)), mn_own(tm(S3)), false, false);    // W P -> S2
-  for (int c0 = 0; c0 < kT; c0 += 32) {                                      // A = sanitize(P - W P)
-    float x[32], y[32];
-    tmem_ld32(S3, c0, x);
-    tmem_ld32(S2, c0, y);
+  for (int c0 = cb; c0 < cb + 64; c0 += 16) {                               // A = sanitize(P - W P)
+    float x[16], y[16];
+    tmem_ld16(S3, c0, x);
+    tmem_ld16(S2, c0, y);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) x[j] = (c0 + j <= t) ? sanitize(x[j] - y[j], clip) : 0.f;
-    tmem_st32(S1, c0, x);
-    st32_f(ainv_g + t * kT + c0, x);
+    for (int j = 0; j < 16; ++j) x[j] = (c0 + j <= t) ? sanitize(x[j] - y[j], clip) : 0.f;
+    tmem_st16(S1, c0, x);
+    st16_f(ainv_g + t * kT + c0, x);
   }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
 
   // ---- 8. wp = A (b k e^gc) -> S0,  u = A (w v) -> S2                          (dot mode) --------
   gemm2(md, pool, mbar, S0, kmaj(tm(S1)), mn_any(src_kb), false, false, S2, kmaj(NoSrc()), mn_any(src_wv), false,
         false, true, false);
-  for (int c0 = 0; c0 < kD; c0 += 32) {
-    float x[32];
-    tmem_ld32(S0, c0, x);
+  for (int c0 = cb; c0 < cb + 64; c0 += 16) {
+    float x[16];
+    tmem_ld16(S0, c0, x);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) x[j] = sanitize(x[j], clip);
-    tmem_st32(S0, c0, x);
-    st32_f(wp_g + t * kD + c0, x);
-    tmem_ld32(S2, c0, x);
+    for (int j = 0; j < 16; ++j) x[j] = sanitize(x[j], clip);
+    tmem_st16(S0, c0, x);
+    st16_f(wp_g + t * kD + c0, x);
+    tmem_ld16(S2, c0, x);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) x[j] = sanitize(x[j], clip);
-    tmem_st32(S2, c0, x);
-    st32_f(u_g + t * kD + c0, x);
+    for (int j = 0; j < 16; ++j) x[j] = sanitize(x[j], clip);
+    tmem_st16(S2, c0, x);
+    st16_f(u_g + t * kD + c0, x);
   }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
 
   // ---- 9. M = diag(e^gl) - kg^T wp -> S1,  Bc = kg^T u -> S3                  (dot mode) --------
   gemm2(md, pool, mbar, S1, mn_any(src_kg), mn_own(tm(S0)), false, false, S3, mn_any(NoSrc()), mn_own(tm(S2)),
         false, false, true, false);
   {
-    const Mode mfm = md;  // the forward scan multiplies in dot mode
     const float dec = ex(fminf(gl_s[t], 0.f));
-    for (int c0 = 0; c0 < kD; c0 += 32) {
-      float x[32];
-      tmem_ld32(S1, c0, x);
+    for (int c0 = cb; c0 < cb + 64; c0 += 16) {
+      float x[16];
+      tmem_ld16(S1, c0, x);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) x[j] = ((c0 + j) == t ? dec : 0.f) - x[j];
-#pragma unroll
-      for (int j = 0; j < 32; j += 8) image_store8(mf_g, mfm, t, c0 + j, x + j);
-      tmem_ld32(S3, c0, x);
-      st32_f(bc_g + t * kD + c0, x);
+      for (int j = 0; j < 16; ++j) x[j] = ((c0 + j) == t ? dec : 0.f) - x[j];
+      image_store8(mf_g, md, t, c0, x);
+      image_store8(mf_g, md, t, c0 + 8, x + 8);
+      tmem_ld16(S3, c0, x);
+      st16_f(bc_g + t * kD + c0, x);
     }
   }
 
@@ -270,7 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_intra_kernel(const OpParams p
 // fwd_out: v_new = u - wp h_pre;  o = sanitize(scale qg h_pre + Aqk v_new)
 // ---------------------------------------------------------------------------------------
 template <class TIn>
-__global__ void __launch_bounds__(kThreads, 1) fwd_out_kernel(const OpParams p, float* __restrict__ o_out) {
+__global__ void __launch_bounds__(kCT, 1) fwd_out_kernel(const OpParams p, float* __restrict__ o_out) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
   const uint32_t pool = smem_u32(sm);
@@ -278,7 +291,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_out_kernel(const OpParams p, 
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kPoolBytes + kGcBytes);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 1);
 
-  const int t = threadIdx.x, warp = t >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int t = crow(), cb = chalf() * 64;
   const int ch = blockIdx.x, bh = ch / p.NC, c = ch % p.NC;
   const long long off = chunk_off(p, bh, c);
   const TIn* q = reinterpret_cast<const TIn*>(p.q) + off;
@@ -297,7 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_out_kernel(const OpParams p, 
     tmem_alloc(tslot, 256);
     tmem_relinquish();
   }
-  if (t == 0) {
+  if (tid == 0) {
     mbar_init(bar, 1);
     fence_mbar_init();
   }
@@ -313,38 +327,41 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_out_kernel(const OpParams p, 
   const uint32_t S0 = tb, S1 = tb + 128;
   MmaBar mbar{bar, 0u, p.status};
 
-  auto src_wp = [&](int r, int c0, float* x) { ld32_f(wp_g + r * kD + c0, x); };
+  auto src_wp = [&](int r, int c0, float* x) { ld16_f(wp_g + r * kD + c0, x); };
   auto src_qg = [&](int r, int c0, float* x) {  // scale sanitize(q e^min(gc, 0))
-    ld32_in(q + r * kD + c0, x);
+    ld16_in(q + r * kD + c0, x);
     const float* gr = gcs + r * kGcPitch + c0;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) x[j] = scale * sanitize(x[j] * ex(fminf(gr[j], 0.f)), clip);
+    for (int j = 0; j < 16; ++j) x[j] = scale * sanitize(x[j] * ex(fminf(gr[j], 0.f)), clip);
   };
-  auto src_h = [&](int r, int c0, float* x) { ld32_f(h_g + r * kD + c0, x); };
-  auto src_aqk = [&](int r, int c0, float* x) { ld32_f(aqk_g + r * kT + c0, x); };
-  auto tm0 = [&](int, int c0, float* x) { tmem_ld32(S0, (uint32_t)c0, x); };
+  auto src_h = [&](int r, int c0, float* x) { ld16_f(h_g + r * kD + c0, x); };
+  auto src_aqk = [&](int r, int c0, float* x) { ld16_f(aqk_g + r * kT + c0, x); };
+  auto tm0 = [&](int, int c0, float* x) { tmem_ld16(S0, (uint32_t)c0, x); };
 
   // S0 = wp h_pre,  S1 = (scale qg) h_pre   (shared B = h_pre)
   gemm2(md, pool, mbar, S0, kmaj(src_wp), mn_any(src_h), false, false, S1, kmaj(src_qg), mn_any(NoSrc()), false,
         false, false, true);
   // v_new = u - S0 (kept in S0 and written as a residual)
-  for (int c0 = 0; c0 < kD; c0 += 32) {
-    float x[32], uv[32];
-    tmem_ld32(S0, c0, x);
-    ld32_f(u_g + t * kD + c0, uv);
+  for (int c0 = cb; c0 < cb + 64; c0 += 16) {
+    float x[16], uv[16];
+    tmem_ld16(S0, c0, x);
+    ld16_f(u_g + t * kD + c0, uv);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) x[j] = uv[j] - x[j];
-    st32_f(vn_g + t * kD + c0, x);
-    tmem_st32(S0, c0, x);
+    for (int j = 0; j < 16; ++j) x[j] = uv[j] - x[j];
+    st16_f(vn_g + t * kD + c0, x);
+    tmem_st16(S0, c0, x);
   }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
   // S1 += Aqk v_new
   gemm1(md, pool, mbar, S1, kmaj(src_aqk), mn_own(tm0), false, true);
-  for (int c0 = 0; c0 < kD; c0 += 32) {
-    float x[32];
-    tmem_ld32(S1, c0, x);
+  for (int c0 = cb; c0 < cb + 64; c0 += 16) {
+    float x[16];
+    tmem_ld16(S1, c0, x);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) x[j] = sanitize(x[j], clip);
-    st32_f(o_g + t * kD + c0, x);
+    for (int j = 0; j < 16; ++j) x[j] = sanitize(x[j], clip);
+    st16_f(o_g + t * kD + c0, x);
   }
   tc_fence_before();
   __syncthreads();
@@ -359,7 +376,7 @@ static cudaError_t launch_fwd_intra_t(const OpParams& p, int nblocks, cudaStream
   cudaError_t e = cudaFuncSetAttribute(fwd_intra_kernel<TIn>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)kIntraSmem);
   if (e != cudaSuccess) return e;
-  fwd_intra_kernel<TIn><<<nblocks, kThreads, kIntraSmem, st>>>(p);
+  fwd_intra_kernel<TIn><<<nblocks, kCT, kIntraSmem, st>>>(p);
   return cudaGetLastError();
 }
 template <class TIn>
@@ -367,7 +384,7 @@ static cudaError_t launch_fwd_out_t(const OpParams& p, float* o, int nblocks, cu
   cudaError_t e =
       cudaFuncSetAttribute(fwd_out_kernel<TIn>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kOutSmem);
   if (e != cudaSuccess) return e;
-  fwd_out_kernel<TIn><<<nblocks, kThreads, kOutSmem, st>>>(p, o);
+  fwd_out_kernel<TIn><<<nblocks, kCT, kOutSmem, st>>>(p, o);
   return cudaGetLastError();
 }
 

@@ -93,6 +93,7 @@ struct MmaBar {
   unsigned* status;
   __device__ __forceinline__ void commit_wait() {
     if (threadIdx.x == 0) mma_commit(bar);
+    __syncwarp();
     mbar_wait(bar, phase, status);
     phase ^= 1u;
     tc_fence_after();
@@ -177,57 +178,62 @@ __device__ __forceinline__ void image_store1(uint8_t* dst, Mode m, int row, int 
   }
 }
 
+// ---------------------------------------------------------------------------
+// Chunk kernels run 256 threads: thread t owns row (t & 127) -- TMEM lane t & 127, reachable by
+// warps w and w + 4 -- and half (t >> 7) of that row's columns.
+// ---------------------------------------------------------------------------
+constexpr int kCT = 256;
+__device__ __forceinline__ int crow() { return threadIdx.x & 127; }
+__device__ __forceinline__ int chalf() { return threadIdx.x >> 7; }
+
 // Column-wise inclusive cumsum of the chunk's gate g (T x D) into shared memory
-// gcs[t * kGcPitch + d].  The chunk is first loaded cooperatively with coalesced 16-byte loads
-// (all threads, many loads in flight), then thread d scans channel d in shared memory.
-// Also returns the channel's max, min and whether a positive gate was seen.
+// gcs[t * kGcPitch + d].  The chunk is loaded cooperatively with coalesced 16-byte loads (all
+// threads, many loads in flight), then thread d < 128 scans channel d in shared memory and
+// returns the channel's max, min and whether a positive gate was seen.
 // (pipeline.py:21 / ref.py:14: gc = cumsum(g) per chunk.)
 constexpr int kGcPitch = 132;  // padded row pitch (floats): conflict-free row reads by row owners
 
 template <class TIn>
 __device__ __forceinline__ void chunk_cumsum(const TIn* __restrict__ g, float* gcs, float& mx, float& mn,
                                              bool& pos) {
-  const int d = threadIdx.x;
-#pragma unroll 16
-  for (int i = d; i < kT * (kD / 4); i += kThreads) {
+  const int tid = threadIdx.x;
+#pragma unroll 8
+  for (int i = tid; i < kT * (kD / 4); i += kCT) {
     const int r = i >> 5, c4 = (i & 31) * 4;
     float v[4];
     ld4(g + r * kD + c4, v);
     *reinterpret_cast<float4*>(gcs + r * kGcPitch + c4) = make_float4(v[0], v[1], v[2], v[3]);
   }
   __syncthreads();
-  float acc = 0.f;
   mx = -3.0e38f;
   mn = 3.0e38f;
   pos = false;
+  if (tid < kD) {
+    float acc = 0.f;
 #pragma unroll 8
-  for (int t = 0; t < kT; ++t) {
-    const float x = gcs[t * kGcPitch + d];
-    pos |= x > 0.f;
-    acc += x;
-    gcs[t * kGcPitch + d] = acc;
-    mx = fmaxf(mx, acc);
-    mn = fminf(mn, acc);
+    for (int t = 0; t < kT; ++t) {
+      const float x = gcs[t * kGcPitch + tid];
+      pos |= x > 0.f;
+      acc += x;
+      gcs[t * kGcPitch + tid] = acc;
+      mx = fmaxf(mx, acc);
+      mn = fminf(mn, acc);
+    }
   }
 }
 
 // ---------------------------------------------------------------------------
-// Generic K-loop over one or two operand pairs (all M = N = 128, K = 128).
-// Operands come from "row sources": src(row, c0, out32) returns 32 consecutive values of row
-// `row` of the source matrix starting at column c0.  A K-major operand (mn = false) is the
-// source itself (row = M/N index, column = K index): every thread stages its own row.  An
-// MN-major operand (mn = true) is the transpose of the source (source row = K index): only the
-// warp(s) whose rows fall in the current K-slice stage.  TMEM-backed sources are warp-collective,
-// which both patterns respect (whole warps call them).
+// Generic K-loop over one or two operand pairs (all M = N = K = 128).
+// Operands come from "row sources": src(row, c0, out16) returns 16 consecutive values of row
+// `row` of the source matrix starting at column c0.
+//   kmaj  : K-major; the source row is the operand's M/N row; every thread stages its own row
+//           (its half of the slice's columns).  Works for TMEM-backed sources.
+//   mn_any: MN-major; the source row is the operand's K row; any thread may fetch any row
+//           (global- or shared-memory-backed sources): (row, 16-column group) items over all
+//           threads.
+//   mn_own: MN-major, TMEM-backed: the two warps owning the slice's lanes stage it, one half of
+//           the MN columns each.
 // ---------------------------------------------------------------------------
-// An operand: how it is laid out for the MMA and who may fetch its rows.
-//   mn  = false: K-major; the source row is the operand's M/N row and every thread stages its own
-//                row (required for TMEM-backed sources, which only the owning lane can read).
-//   mn  = true : MN-major; the source row is the operand's K row.
-//   any = true : any thread may fetch any row (global- or shared-memory-backed sources): an
-//                MN-major slice is then staged by all threads, (row, 32-column group) items.
-//   any = false: only the owning warp may fetch a row (TMEM-backed): the warp(s) whose rows lie in
-//                the slice stage it.
 template <class Src>
 struct Opnd {
   bool mn, any;
@@ -240,30 +246,36 @@ __device__ __forceinline__ Opnd<Src> mn_any(Src s) { return Opnd<Src>{true, true
 template <class Src>
 __device__ __forceinline__ Opnd<Src> mn_own(Src s) { return Opnd<Src>{true, false, s}; }
 
-template <class Src>
-__device__ __forceinline__ void stage_op(const Tile tt[2], const Opnd<Src>& op, Mode m, int k0, int KS) {
-  const int t = threadIdx.x, warp = t >> 5;
-  const bool lo = m.passes == 3;
+template <int FMT, class Src>
+__device__ __forceinline__ void stage_op_t(const Tile tt[2], const Opnd<Src>& op, bool lo, int k0, int KS) {
+  const int row = crow(), half = chalf(), warp = threadIdx.x >> 5;
   if (!op.mn) {
-    for (int i = 0; i < KS; i += 32) {
-      float x[32];
-      op.src(t, k0 + i, x);
-      stage_krow(tt[0], tt[1], lo, m.fmt, (uint32_t)t, i, x, 32);
+    const int hw = KS >> 1;
+    for (int i = half * hw; i < (half + 1) * hw; i += 16) {
+      float x[16];
+      op.src(row, k0 + i, x);
+      stage_krow_t<FMT, 16>(tt[0], tt[1], lo, (uint32_t)row, i, x);
     }
   } else if (op.any) {
-    for (int it = t; it < KS * 4; it += kThreads) {
-      const int r = it % KS, c0 = (it / KS) * 32;
-      float x[32];
+    for (int it = threadIdx.x; it < KS * 8; it += kCT) {
+      const int r = it % KS, c0 = (it / KS) * 16;
+      float x[16];
       op.src(k0 + r, c0, x);
-      stage_mnrow(tt[0], tt[1], lo, m.fmt, (uint32_t)r, c0, x, 32);
+      stage_mnrow_t<FMT, 16>(tt[0], tt[1], lo, (uint32_t)r, c0, x);
     }
-  } else if (warp * 32 >= k0 && warp * 32 < k0 + KS) {
-    for (int c0 = 0; c0 < 128; c0 += 32) {
-      float x[32];
-      op.src(t, c0, x);
-      stage_mnrow(tt[0], tt[1], lo, m.fmt, (uint32_t)(t - k0), c0, x, 32);
+  } else if ((warp & 3) * 32 >= k0 && (warp & 3) * 32 < k0 + KS) {
+#pragma unroll 1
+    for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 16) {
+      float x[16];
+      op.src(row, c0, x);
+      stage_mnrow_t<FMT, 16>(tt[0], tt[1], lo, (uint32_t)(row - k0), c0, x);
     }
   }
+}
+template <class Src>
+__device__ __forceinline__ void stage_op(const Tile tt[2], const Opnd<Src>& op, Mode m, int k0, int KS) {
+  if (m.fmt == kTF32) stage_op_t<kTF32>(tt, op, m.passes == 3, k0, KS);
+  else stage_op_t<kBF16>(tt, op, m.passes == 3, k0, KS);
 }
 
 struct NoSrc {
@@ -325,27 +337,32 @@ __device__ __forceinline__ void gemm2(Mode m, uint32_t pool, MmaBar& mb, uint32_
   }
 }
 
-// Row sources
+// Row loaders (16 values)
 template <class TIn>
-__device__ __forceinline__ void ld32_in(const TIn* p, float* x) {
+__device__ __forceinline__ void ld16_in(const TIn* p, float* x) {
 #pragma unroll
-  for (int j = 0; j < 32; j += 4) ld4(p + j, x + j);
+  for (int j = 0; j < 16; j += 4) ld4(p + j, x + j);
 }
-__device__ __forceinline__ void ld32_f(const float* p, float* x) {
+__device__ __forceinline__ void ld16_f(const float* p, float* x) {
 #pragma unroll
-  for (int j = 0; j < 32; j += 4) {
+  for (int j = 0; j < 16; j += 4) {
     float4 v = *reinterpret_cast<const float4*>(p + j);
     x[j] = v.x; x[j + 1] = v.y; x[j + 2] = v.z; x[j + 3] = v.w;
   }
 }
-__device__ __forceinline__ void st32_f(float* p, const float* x) {
+__device__ __forceinline__ void st16_f(float* p, const float* x) {
 #pragma unroll
-  for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(p + j) = make_float4(x[j], x[j + 1], x[j + 2], x[j + 3]);
+  for (int j = 0; j < 16; j += 4) *reinterpret_cast<float4*>(p + j) = make_float4(x[j], x[j + 1], x[j + 2], x[j + 3]);
 }
-__device__ __forceinline__ void st32_out(float* p, const float* x) { st32_f(p, x); }
-__device__ __forceinline__ void st32_out(__nv_bfloat16* p, const float* x) {
+__device__ __forceinline__ void st16_out(float* p, const float* x) { st16_f(p, x); }
+__device__ __forceinline__ void st16_out(__nv_bfloat16* p, const float* x) {
 #pragma unroll
-  for (int j = 0; j < 32; j += 4) st4(p + j, x + j);
+  for (int j = 0; j < 16; j += 4) st4(p + j, x + j);
+}
+// the 32-wide forms used by the scan / host-side helpers
+__device__ __forceinline__ void ld32_f(const float* p, float* x) {
+  ld16_f(p, x);
+  ld16_f(p + 16, x + 16);
 }
 
 constexpr int kDV = 32;  // state columns per scan CTA

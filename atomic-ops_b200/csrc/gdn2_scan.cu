@@ -110,6 +110,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanParams sp) 
       mma_tiles(m.fmt, m.passes, tb, A, Bt, kDV, nsteps, false, false);
       mma_commit(bar_mma);
     }
+    __syncwarp();  // park warp 0's other lanes here while lane 0 issues, instead of polling the barrier
     mbar_wait(bar_mma, ph_mma, sp.status);
     ph_mma ^= 1u;
     tc_fence_after();
