@@ -246,24 +246,35 @@ __device__ __forceinline__ Opnd<Src> mn_any(Src s) { return Opnd<Src>{true, true
 template <class Src>
 __device__ __forceinline__ Opnd<Src> mn_own(Src s) { return Opnd<Src>{true, false, s}; }
 
-template <int FMT, class Src>
-__device__ __forceinline__ void stage_op_t(const Tile tt[2], const Opnd<Src>& op, bool lo, int k0, int KS) {
-  const int row = crow(), half = chalf(), warp = threadIdx.x >> 5;
+// Work items of one operand slice (KS elements of K) for this thread: kmaj and mn_any operands
+// both give every thread KS / 32 items of 16 values.
+//   kmaj  : item p = columns [k0 + half * KS/2 + 16 p, +16) of the thread's own row
+//   mn_any: item p = (row r, 16-column group) with it = tid + 256 p, r = it % KS, c0 = (it / KS) * 16
+template <class Src>
+__device__ __forceinline__ void fetch_item(const Opnd<Src>& op, int k0, int KS, int p, float* x) {
   if (!op.mn) {
-    const int hw = KS >> 1;
-    for (int i = half * hw; i < (half + 1) * hw; i += 16) {
-      float x[16];
-      op.src(row, k0 + i, x);
-      stage_krow_t<FMT, 16>(tt[0], tt[1], lo, (uint32_t)row, i, x);
-    }
+    op.src(crow(), k0 + chalf() * (KS >> 1) + p * 16, x);
   } else if (op.any) {
-    for (int it = threadIdx.x; it < KS * 8; it += kCT) {
-      const int r = it % KS, c0 = (it / KS) * 16;
-      float x[16];
-      op.src(k0 + r, c0, x);
-      stage_mnrow_t<FMT, 16>(tt[0], tt[1], lo, (uint32_t)r, c0, x);
-    }
-  } else if ((warp & 3) * 32 >= k0 && (warp & 3) * 32 < k0 + KS) {
+    const int it = threadIdx.x + p * kCT;
+    op.src(k0 + it % KS, (it / KS) * 16, x);
+  }
+}
+template <int FMT, class Src>
+__device__ __forceinline__ void store_item(const Tile tt[2], const Opnd<Src>& op, bool lo, int KS, int p,
+                                           const float* x) {
+  if (!op.mn) {
+    stage_krow_t<FMT, 16>(tt[0], tt[1], lo, (uint32_t)crow(), chalf() * (KS >> 1) + p * 16, x);
+  } else if (op.any) {
+    const int it = threadIdx.x + p * kCT;
+    stage_mnrow_t<FMT, 16>(tt[0], tt[1], lo, (uint32_t)(it % KS), (it / KS) * 16, x);
+  }
+}
+// TMEM-backed MN-major operands: the two warps owning the slice's lanes, one half of MN each.
+template <int FMT, class Src>
+__device__ __forceinline__ void stage_own(const Tile tt[2], const Opnd<Src>& op, bool lo, int k0, int KS) {
+  const int warp = threadIdx.x >> 5;
+  if (op.mn && !op.any && (warp & 3) * 32 >= k0 && (warp & 3) * 32 < k0 + KS) {
+    const int row = crow(), half = chalf();
 #pragma unroll 1
     for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 16) {
       float x[16];
@@ -272,10 +283,80 @@ __device__ __forceinline__ void stage_op_t(const Tile tt[2], const Opnd<Src>& op
     }
   }
 }
-template <class Src>
-__device__ __forceinline__ void stage_op(const Tile tt[2], const Opnd<Src>& op, Mode m, int k0, int KS) {
-  if (m.fmt == kTF32) stage_op_t<kTF32>(tt, op, m.passes == 3, k0, KS);
-  else stage_op_t<kBF16>(tt, op, m.passes == 3, k0, KS);
+
+// Register buffer for the prefetched items of one slice: up to two items (KS / 32) of two operands.
+struct Prefetch {
+  float x[2][2][16];
+};
+template <class S1, class S2>
+__device__ __forceinline__ void prefetch2(Prefetch& pf, const Opnd<S1>& o1, const Opnd<S2>& o2, int k0, int KS) {
+  const int np = KS / 32;
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+    if (p < np) {
+      fetch_item(o1, k0, KS, p, pf.x[0][p]);
+      fetch_item(o2, k0, KS, p, pf.x[1][p]);
+    }
+  }
+}
+template <int FMT, class S1, class S2>
+__device__ __forceinline__ void store2_t(const Prefetch& pf, const Tile* t1, const Opnd<S1>& o1, const Tile* t2,
+                                         const Opnd<S2>& o2, bool lo, int KS) {
+  const int np = KS / 32;
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+    if (p < np) {
+      store_item<FMT>(t1, o1, lo, KS, p, pf.x[0][p]);
+      store_item<FMT>(t2, o2, lo, KS, p, pf.x[1][p]);
+    }
+  }
+}
+// Stage operands 3 and 4 (not prefetched) of one slice: loads of both issued before the stores.
+template <int FMT, class S3, class S4>
+__device__ __forceinline__ void stage34_t(const Tile* t3, const Opnd<S3>& o3, const Tile* t4, const Opnd<S4>& o4,
+                                          int nops, bool lo, int k0, int KS) {
+  const int np = KS / 32;
+#pragma unroll 1
+  for (int p = 0; p < np; ++p) {
+    float x3[16], x4[16];
+    if (nops > 2) fetch_item(o3, k0, KS, p, x3);
+    if (nops > 3) fetch_item(o4, k0, KS, p, x4);
+    if (nops > 2) store_item<FMT>(t3, o3, lo, KS, p, x3);
+    if (nops > 3) store_item<FMT>(t4, o4, lo, KS, p, x4);
+  }
+}
+
+// One K-loop of up to four operands (ops 1-2: pair 1's A and B, or A1 and the shared B; ops 3-4:
+// the rest).  Software-pipelined: the global / shared loads of ops 1-2 for slice s+1 are issued
+// right after slice s's MMAs, so their latency overlaps the tensor core; TMEM-backed MN-major
+// operands are staged in the slice itself (TMEM loads are short).
+template <int FMT, class S1, class S2, class S3, class S4, class Issue>
+__device__ __forceinline__ void kloop_t(MmaBar& mb, const Tile* t1, const Opnd<S1>& o1, const Tile* t2,
+                                        const Opnd<S2>& o2, const Tile* t3, const Opnd<S3>& o3, const Tile* t4,
+                                        const Opnd<S4>& o4, int nops, bool lo, int KS, Issue issue) {
+  const int ns = 128 / KS;
+  Prefetch pf;
+  prefetch2(pf, o1, o2, 0, KS);
+  for (int s = 0; s < ns; ++s) {
+    const int k0 = s * KS;
+    store2_t<FMT>(pf, t1, o1, t2, o2, lo, KS);
+    stage34_t<FMT>(t3, o3, t4, o4, nops, lo, k0, KS);
+    stage_own<FMT>(t1, o1, lo, k0, KS);
+    stage_own<FMT>(t2, o2, lo, k0, KS);
+    if (nops > 2) stage_own<FMT>(t3, o3, lo, k0, KS);
+    if (nops > 3) stage_own<FMT>(t4, o4, lo, k0, KS);
+    staged_sync();
+    if (threadIdx.x == 0) {
+      tc_fence_after();
+      issue(s);
+      mma_commit(mb.bar);
+    }
+    __syncwarp();
+    if (s + 1 < ns) prefetch2(pf, o1, o2, k0 + KS, KS);
+    mbar_wait(mb.bar, mb.phase, mb.status);
+    mb.phase ^= 1u;
+    tc_fence_after();
+  }
 }
 
 struct NoSrc {
@@ -286,23 +367,16 @@ struct NoSrc {
 template <class SA, class SB>
 __device__ __forceinline__ void gemm1(Mode m, uint32_t pool, MmaBar& mb, uint32_t d, const Opnd<SA>& a,
                                       const Opnd<SB>& b, bool neg, bool acc) {
-  const int KS = kslice(m), ns = 128 / KS;
-  for (int s = 0; s < ns; ++s) {
-    const int k0 = s * KS;
-    Tile A[2], B[2];
-    A[0] = a.mn ? pool_mn(pool, 0, m) : pool_k(pool, 0);
-    A[1] = a.mn ? pool_mn(pool, 1, m) : pool_k(pool, 1);
-    B[0] = b.mn ? pool_mn(pool, 2, m) : pool_k(pool, 2);
-    B[1] = b.mn ? pool_mn(pool, 3, m) : pool_k(pool, 3);
-    stage_op(A, a, m, k0, KS);
-    stage_op(B, b, m, k0, KS);
-    staged_sync();
-    if (threadIdx.x == 0) {
-      tc_fence_after();
-      issue_slice(m, d, A, B, 128, neg, acc || s > 0);
-    }
-    mb.commit_wait();
-  }
+  const int KS = kslice(m);
+  Tile A[2], B[2];
+  A[0] = a.mn ? pool_mn(pool, 0, m) : pool_k(pool, 0);
+  A[1] = a.mn ? pool_mn(pool, 1, m) : pool_k(pool, 1);
+  B[0] = b.mn ? pool_mn(pool, 2, m) : pool_k(pool, 2);
+  B[1] = b.mn ? pool_mn(pool, 3, m) : pool_k(pool, 3);
+  auto issue = [&](int s) { issue_slice(m, d, A, B, 128, neg, acc || s > 0); };
+  const bool lo = m.passes == 3;
+  if (m.fmt == kTF32) kloop_t<kTF32>(mb, A, a, B, b, A, a, B, b, 2, lo, KS, issue);
+  else kloop_t<kBF16>(mb, A, a, B, b, A, a, B, b, 2, lo, KS, issue);
 }
 
 // Two products sharing the K-slicing: D1 (+)= A1 B1 and D2 (+)= A2 B2, where pair 2 reuses pair 1's
@@ -312,28 +386,30 @@ __device__ __forceinline__ void gemm2(Mode m, uint32_t pool, MmaBar& mb, uint32_
                                       const Opnd<SB1>& b1, bool neg1, bool acc1, uint32_t d2,
                                       const Opnd<SA2>& a2, const Opnd<SB2>& b2, bool neg2, bool acc2,
                                       bool share_a, bool share_b) {
-  const int KS = kslice(m), ns = 128 / KS;
+  const int KS = kslice(m);
   auto tiles = [&](int i, bool mn, Tile out[2]) {
     out[0] = mn ? pool_mn(pool, i, m) : pool_k(pool, i);
     out[1] = mn ? pool_mn(pool, i + 1, m) : pool_k(pool, i + 1);
   };
-  for (int s = 0; s < ns; ++s) {
-    const int k0 = s * KS;
-    Tile A1[2], B1[2], A2[2], B2[2];
-    tiles(0, a1.mn, A1);
-    tiles(2, b1.mn, B1);
-    int nt = 4;
-    stage_op(A1, a1, m, k0, KS);
-    stage_op(B1, b1, m, k0, KS);
-    if (share_a) { A2[0] = A1[0]; A2[1] = A1[1]; } else { tiles(nt, a2.mn, A2); nt += 2; stage_op(A2, a2, m, k0, KS); }
-    if (share_b) { B2[0] = B1[0]; B2[1] = B1[1]; } else { tiles(nt, b2.mn, B2); nt += 2; stage_op(B2, b2, m, k0, KS); }
-    staged_sync();
-    if (threadIdx.x == 0) {
-      tc_fence_after();
-      issue_slice(m, d1, A1, B1, 128, neg1, acc1 || s > 0);
-      issue_slice(m, d2, A2, B2, 128, neg2, acc2 || s > 0);
-    }
-    mb.commit_wait();
+  Tile A1[2], B1[2], A2[2], B2[2];
+  tiles(0, a1.mn, A1);
+  tiles(2, b1.mn, B1);
+  int nt = 4;
+  if (share_a) { A2[0] = A1[0]; A2[1] = A1[1]; } else { tiles(nt, a2.mn, A2); nt += 2; }
+  if (share_b) { B2[0] = B1[0]; B2[1] = B1[1]; } else { tiles(nt, b2.mn, B2); nt += 2; }
+  auto issue = [&](int s) {
+    issue_slice(m, d1, A1, B1, 128, neg1, acc1 || s > 0);
+    issue_slice(m, d2, A2, B2, 128, neg2, acc2 || s > 0);
+  };
+  const bool lo = m.passes == 3;
+  if (m.fmt == kTF32) {
+    if (share_a) kloop_t<kTF32>(mb, A1, a1, B1, b1, B2, b2, B2, b2, 3, lo, KS, issue);
+    else if (share_b) kloop_t<kTF32>(mb, A1, a1, B1, b1, A2, a2, A2, a2, 3, lo, KS, issue);
+    else kloop_t<kTF32>(mb, A1, a1, B1, b1, A2, a2, B2, b2, 4, lo, KS, issue);
+  } else {
+    if (share_a) kloop_t<kBF16>(mb, A1, a1, B1, b1, B2, b2, B2, b2, 3, lo, KS, issue);
+    else if (share_b) kloop_t<kBF16>(mb, A1, a1, B1, b1, A2, a2, A2, a2, 3, lo, KS, issue);
+    else kloop_t<kBF16>(mb, A1, a1, B1, b1, A2, a2, B2, b2, 4, lo, KS, issue);
   }
 }
 
