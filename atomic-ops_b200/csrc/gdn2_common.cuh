@@ -369,24 +369,55 @@ __device__ __forceinline__ uint64_t tdesc(const Tile& t, int kstep) {
   return sdesc(t.addr + (uint32_t)kstep * t.step, t.lbo, t.sbo) | ((uint64_t)t.ltype << 61);
 }
 
+// One MMA with a compile-time operand kind.
+template <int FMT>
+__device__ __forceinline__ void mma_t(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t id, uint32_t accumulate) {
+  if constexpr (FMT == kTF32) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(id), "r"(accumulate)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(id), "r"(accumulate)
+        : "memory");
+  }
+}
+
 // Issue D (+)= A * B over `nsteps` MMA K-steps with the given number of precision passes.
 // a[0]/b[0] are the hi parts, a[1]/b[1] the lo parts (used only when passes == 3).
-// Pass order puts the small cross terms first.
-__device__ __forceinline__ void mma_tiles(int fmt, int passes, uint32_t d_tmem, const Tile a[2], const Tile b[2],
-                                          int N, int nsteps, bool neg_a, bool accumulate) {
-  const uint32_t id = idesc(fmt, N, a[0].mn, b[0].mn, neg_a);
+// Descriptors are formed once; a K-step advances the 14-bit start-address field by step/16
+// (shared-memory addresses stay below 256 KB, so the field never carries).  Small cross terms
+// are accumulated first.
+template <int FMT>
+__device__ __forceinline__ void mma_tiles_t(int passes, uint32_t d_tmem, const Tile a[2], const Tile b[2], int N,
+                                            int nsteps, bool neg_a, bool accumulate) {
+  const uint32_t id = idesc(FMT, N, a[0].mn, b[0].mn, neg_a);
+  const uint64_t ah = tdesc(a[0], 0), bh = tdesc(b[0], 0);
+  const uint64_t ia = a[0].step >> 4, ib = b[0].step >> 4;
   uint32_t acc = accumulate ? 1u : 0u;
   if (passes == 3) {
+    const uint64_t al = tdesc(a[1], 0), bl = tdesc(b[1], 0);
+#pragma unroll 4
     for (int s = 0; s < nsteps; ++s) {
-      mma_issue(fmt, d_tmem, tdesc(a[0], s), tdesc(b[1], s), id, acc);
+      mma_t<FMT>(d_tmem, ah + s * ia, bl + s * ib, id, acc);
       acc = 1u;
-      mma_issue(fmt, d_tmem, tdesc(a[1], s), tdesc(b[0], s), id, 1u);
+      mma_t<FMT>(d_tmem, al + s * ia, bh + s * ib, id, 1u);
     }
   }
+#pragma unroll 4
   for (int s = 0; s < nsteps; ++s) {
-    mma_issue(fmt, d_tmem, tdesc(a[0], s), tdesc(b[0], s), id, acc);
+    mma_t<FMT>(d_tmem, ah + s * ia, bh + s * ib, id, acc);
     acc = 1u;
   }
+}
+__device__ __forceinline__ void mma_tiles(int fmt, int passes, uint32_t d_tmem, const Tile a[2], const Tile b[2], int N,
+                                          int nsteps, bool neg_a, bool accumulate) {
+  if (fmt == kTF32) mma_tiles_t<kTF32>(passes, d_tmem, a, b, N, nsteps, neg_a, accumulate);
+  else mma_tiles_t<kBF16>(passes, d_tmem, a, b, N, nsteps, neg_a, accumulate);
 }
 
 // --- writing operand values (one 16-byte piece at a time) -------------------
