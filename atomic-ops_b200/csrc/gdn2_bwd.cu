@@ -35,7 +35,7 @@ __device__ __forceinline__ uint8_t* align1024b(uint8_t* p) {
 // bwd_pre: dvl = Aqk^T do,  Cc = scale qg^T do - wp^T dvl, and the transposed transition
 // image M^T = diag(e^gl) - wp^T kg of the reverse scan      (b3_dot_mode, mega.py:31-34)
 // ---------------------------------------------------------------------------------------
-template <class TIn>
+template <class TIn, int B3>
 __global__ void __launch_bounds__(kCT, 1) bwd_pre_kernel(const BwdParams P) {
   extern __shared__ uint8_t smem_raw[];
   const OpParams& p = P.op;
@@ -59,7 +59,7 @@ __global__ void __launch_bounds__(kCT, 1) bwd_pre_kernel(const BwdParams P) {
   float* dvl_g = reinterpret_cast<float*>(P.ws + P.wl.dvl) + (size_t)ch * mat;
   float* cc_g = reinterpret_cast<float*>(P.ws + P.wl.cc) + (size_t)ch * mat;
   uint8_t* mb_g = P.ws + P.wl.mb + (size_t)ch * P.wl.mb_stride;
-  const Mode m3 = mode_from_enum(p.b3_mode);
+  const Mode m3 = mode_from_enum(B3 >= 0 ? B3 : p.b3_mode);
   const float clip = p.clip, scale = p.scale;
 
   if (warp == 0) {
@@ -136,7 +136,7 @@ __global__ void __launch_bounds__(kCT, 1) bwd_pre_kernel(const BwdParams P) {
 // ---------------------------------------------------------------------------------------
 // bwd_intra
 // ---------------------------------------------------------------------------------------
-template <class TIn>
+template <class TIn, int B3>
 __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
   extern __shared__ uint8_t smem_raw[];
   const OpParams& p = P.op;
@@ -173,7 +173,7 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
   const float* vnew_g = reinterpret_cast<const float*>(p.res + p.rl.vnew) + (size_t)ch * mat;
   const float* dvl_g = reinterpret_cast<const float*>(P.ws + P.wl.dvl) + (size_t)ch * mat;
   const float* dhn_g = reinterpret_cast<const float*>(P.ws + P.wl.dhs) + (size_t)ch * mat;
-  const Mode m3 = mode_from_enum(p.b3_mode);
+  const Mode m3 = mode_from_enum(B3 >= 0 ? B3 : p.b3_mode);
   const Mode mh = mode_from_enum(GDN2_PREC_HIGHEST);  // B4 products are fixed at "highest" (mega.py:13)
   const float clip = p.clip, scale = p.scale;
 
@@ -435,27 +435,41 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
   if (warp == 0) tmem_dealloc(tb, 512);
 }
 
-template <class TIn>
+template <class TIn, int B3>
 static cudaError_t launch_bwd_pre_t(const BwdParams& p, int nblocks, cudaStream_t st) {
-  cudaError_t e = cudaFuncSetAttribute(bwd_pre_kernel<TIn>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPreSmem);
+  cudaError_t e =
+      cudaFuncSetAttribute(bwd_pre_kernel<TIn, B3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPreSmem);
   if (e != cudaSuccess) return e;
-  bwd_pre_kernel<TIn><<<nblocks, kCT, kPreSmem, st>>>(p);
+  bwd_pre_kernel<TIn, B3><<<nblocks, kCT, kPreSmem, st>>>(p);
   return cudaGetLastError();
 }
-template <class TIn>
+template <class TIn, int B3>
 static cudaError_t launch_bwd_intra_t(const BwdParams& p, int nblocks, cudaStream_t st) {
   cudaError_t e =
-      cudaFuncSetAttribute(bwd_intra_kernel<TIn>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBwdSmem);
+      cudaFuncSetAttribute(bwd_intra_kernel<TIn, B3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBwdSmem);
   if (e != cudaSuccess) return e;
-  bwd_intra_kernel<TIn><<<nblocks, kCT, kBwdSmem, st>>>(p);
+  bwd_intra_kernel<TIn, B3><<<nblocks, kCT, kBwdSmem, st>>>(p);
   return cudaGetLastError();
+}
+// Compile-time precision for the reference's default B3 mode (bf16x3) and the all-bf16 mode.
+template <class TIn>
+static cudaError_t launch_bwd_pre_m(const BwdParams& p, int nblocks, cudaStream_t st) {
+  if (p.op.b3_mode == GDN2_PREC_BF16X3) return launch_bwd_pre_t<TIn, GDN2_PREC_BF16X3>(p, nblocks, st);
+  if (p.op.b3_mode == GDN2_PREC_DEFAULT) return launch_bwd_pre_t<TIn, GDN2_PREC_DEFAULT>(p, nblocks, st);
+  return launch_bwd_pre_t<TIn, -1>(p, nblocks, st);
+}
+template <class TIn>
+static cudaError_t launch_bwd_intra_m(const BwdParams& p, int nblocks, cudaStream_t st) {
+  if (p.op.b3_mode == GDN2_PREC_BF16X3) return launch_bwd_intra_t<TIn, GDN2_PREC_BF16X3>(p, nblocks, st);
+  if (p.op.b3_mode == GDN2_PREC_DEFAULT) return launch_bwd_intra_t<TIn, GDN2_PREC_DEFAULT>(p, nblocks, st);
+  return launch_bwd_intra_t<TIn, -1>(p, nblocks, st);
 }
 
 cudaError_t launch_bwd_pre(const BwdParams& p, bool bf16, int nblocks, cudaStream_t st) {
-  return bf16 ? launch_bwd_pre_t<__nv_bfloat16>(p, nblocks, st) : launch_bwd_pre_t<float>(p, nblocks, st);
+  return bf16 ? launch_bwd_pre_m<__nv_bfloat16>(p, nblocks, st) : launch_bwd_pre_m<float>(p, nblocks, st);
 }
 cudaError_t launch_bwd_intra(const BwdParams& p, bool bf16, int nblocks, cudaStream_t st) {
-  return bf16 ? launch_bwd_intra_t<__nv_bfloat16>(p, nblocks, st) : launch_bwd_intra_t<float>(p, nblocks, st);
+  return bf16 ? launch_bwd_intra_m<__nv_bfloat16>(p, nblocks, st) : launch_bwd_intra_m<float>(p, nblocks, st);
 }
 
 }  // namespace gdn2

@@ -41,7 +41,7 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
 // ---------------------------------------------------------------------------------------
 // fwd_intra
 // ---------------------------------------------------------------------------------------
-template <class TIn>
+template <class TIn, int DOT, int SOLVE>
 __global__ void __launch_bounds__(kCT, 1) fwd_intra_kernel(const OpParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
@@ -72,8 +72,8 @@ __global__ void __launch_bounds__(kCT, 1) fwd_intra_kernel(const OpParams p) {
   float* bc_g = reinterpret_cast<float*>(p.res + p.rl.bc) + (size_t)ch * mat;
   uint8_t* mf_g = p.res + p.rl.mf + (size_t)ch * p.rl.mf_stride;
 
-  const Mode md = mode_from_enum(p.dot_mode);
-  const Mode ms = mode_from_enum(p.solve_mode);
+  const Mode md = mode_from_enum(DOT >= 0 ? DOT : p.dot_mode);
+  const Mode ms = mode_from_enum(SOLVE >= 0 ? SOLVE : p.solve_mode);
   const float clip = p.clip;
 
   if (warp == 0) {
@@ -282,7 +282,7 @@ __global__ void __launch_bounds__(kCT, 1) fwd_intra_kernel(const OpParams p) {
 // ---------------------------------------------------------------------------------------
 // fwd_out: v_new = u - wp h_pre;  o = sanitize(scale qg h_pre + Aqk v_new)
 // ---------------------------------------------------------------------------------------
-template <class TIn>
+template <class TIn, int DOT>
 __global__ void __launch_bounds__(kCT, 1) fwd_out_kernel(const OpParams p, float* __restrict__ o_out) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
@@ -304,7 +304,7 @@ __global__ void __launch_bounds__(kCT, 1) fwd_out_kernel(const OpParams p, float
   const float* h_g = reinterpret_cast<const float*>(p.res + p.rl.hs) + ((size_t)bh * (p.NC + 1) + c) * mat;
   float* vn_g = reinterpret_cast<float*>(p.res + p.rl.vnew) + (size_t)ch * mat;
   float* o_g = o_out + off;
-  const Mode md = mode_from_enum(p.dot_mode);
+  const Mode md = mode_from_enum(DOT >= 0 ? DOT : p.dot_mode);
   const float clip = p.clip, scale = p.scale;
 
   if (warp == 0) {
@@ -371,28 +371,44 @@ __global__ void __launch_bounds__(kCT, 1) fwd_out_kernel(const OpParams p, float
 // ---------------------------------------------------------------------------------------
 // Host-side launchers
 // ---------------------------------------------------------------------------------------
-template <class TIn>
+// Kernels are compiled with compile-time precision modes for the configurations that matter
+// (the reference's defaults and the all-bf16 mode), and with runtime modes for the rest (-1).
+template <class TIn, int DOT, int SOLVE>
 static cudaError_t launch_fwd_intra_t(const OpParams& p, int nblocks, cudaStream_t st) {
-  cudaError_t e = cudaFuncSetAttribute(fwd_intra_kernel<TIn>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  cudaError_t e = cudaFuncSetAttribute(fwd_intra_kernel<TIn, DOT, SOLVE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)kIntraSmem);
   if (e != cudaSuccess) return e;
-  fwd_intra_kernel<TIn><<<nblocks, kCT, kIntraSmem, st>>>(p);
+  fwd_intra_kernel<TIn, DOT, SOLVE><<<nblocks, kCT, kIntraSmem, st>>>(p);
+  return cudaGetLastError();
+}
+template <class TIn, int DOT>
+static cudaError_t launch_fwd_out_t(const OpParams& p, float* o, int nblocks, cudaStream_t st) {
+  cudaError_t e = cudaFuncSetAttribute(fwd_out_kernel<TIn, DOT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)kOutSmem);
+  if (e != cudaSuccess) return e;
+  fwd_out_kernel<TIn, DOT><<<nblocks, kCT, kOutSmem, st>>>(p, o);
   return cudaGetLastError();
 }
 template <class TIn>
-static cudaError_t launch_fwd_out_t(const OpParams& p, float* o, int nblocks, cudaStream_t st) {
-  cudaError_t e =
-      cudaFuncSetAttribute(fwd_out_kernel<TIn>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kOutSmem);
-  if (e != cudaSuccess) return e;
-  fwd_out_kernel<TIn><<<nblocks, kCT, kOutSmem, st>>>(p, o);
-  return cudaGetLastError();
+static cudaError_t launch_fwd_intra_m(const OpParams& p, int nblocks, cudaStream_t st) {
+  if (p.dot_mode == GDN2_PREC_HIGHEST && p.solve_mode == GDN2_PREC_BF16X3)
+    return launch_fwd_intra_t<TIn, GDN2_PREC_HIGHEST, GDN2_PREC_BF16X3>(p, nblocks, st);
+  if (p.dot_mode == GDN2_PREC_DEFAULT && p.solve_mode == GDN2_PREC_DEFAULT)
+    return launch_fwd_intra_t<TIn, GDN2_PREC_DEFAULT, GDN2_PREC_DEFAULT>(p, nblocks, st);
+  return launch_fwd_intra_t<TIn, -1, -1>(p, nblocks, st);
+}
+template <class TIn>
+static cudaError_t launch_fwd_out_m(const OpParams& p, float* o, int nblocks, cudaStream_t st) {
+  if (p.dot_mode == GDN2_PREC_HIGHEST) return launch_fwd_out_t<TIn, GDN2_PREC_HIGHEST>(p, o, nblocks, st);
+  if (p.dot_mode == GDN2_PREC_DEFAULT) return launch_fwd_out_t<TIn, GDN2_PREC_DEFAULT>(p, o, nblocks, st);
+  return launch_fwd_out_t<TIn, -1>(p, o, nblocks, st);
 }
 
 cudaError_t launch_fwd_intra(const OpParams& p, bool bf16, int nblocks, cudaStream_t st) {
-  return bf16 ? launch_fwd_intra_t<__nv_bfloat16>(p, nblocks, st) : launch_fwd_intra_t<float>(p, nblocks, st);
+  return bf16 ? launch_fwd_intra_m<__nv_bfloat16>(p, nblocks, st) : launch_fwd_intra_m<float>(p, nblocks, st);
 }
 cudaError_t launch_fwd_out(const OpParams& p, bool bf16, float* o, int nblocks, cudaStream_t st) {
-  return bf16 ? launch_fwd_out_t<__nv_bfloat16>(p, o, nblocks, st) : launch_fwd_out_t<float>(p, o, nblocks, st);
+  return bf16 ? launch_fwd_out_m<__nv_bfloat16>(p, o, nblocks, st) : launch_fwd_out_m<float>(p, o, nblocks, st);
 }
 
 }  // namespace gdn2
