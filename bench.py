@@ -48,22 +48,25 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--dtype", default="fp32", choices=["fp32", "bf16"])
+    ap.add_argument("--sweep", action="store_true",
+                    help="instead of the headline line, print one line per sweep shape (BASELINE configs 3 and 4)")
     return ap.parse_args()
 
 
 # --------------------------------------------------------------------------------------
 # inputs (BASELINE config 2 distributions, generated on the device)
 # --------------------------------------------------------------------------------------
-def make_inputs(seed, device, dtype):
+def make_inputs(seed, device, dtype, shape=(B, H, L)):
     gen = torch.Generator(device=device).manual_seed(seed)
     n = lambda *s: torch.randn(*s, generator=gen, device=device, dtype=torch.float32)
     l2 = lambda x: x / torch.sqrt((x * x).sum(-1, keepdim=True) + 1e-6)
-    sh = (B, H, L, D)
+    nb, nh, nl = shape
+    sh = (nb, nh, nl, D)
     q, k, w = l2(n(*sh)), l2(n(*sh)), l2(n(*sh))
     v = n(*sh)
     b = torch.sigmoid(n(*sh))
     g = torch.nn.functional.logsigmoid(n(*sh) + 3.0)
-    h0 = n(B, H, D, D) * 0.01
+    h0 = n(nb, nh, D, D) * 0.01
     return [t.to(dtype).contiguous() for t in (q, k, v, w, b, g)], h0.contiguous()
 
 
@@ -364,8 +367,85 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+# --------------------------------------------------------------------------------------
+# sweep (B4, H in {2,4,6}, L in {2048,4096}, fwd-only and fwd+bwd;
+# config 4: B1 H6 L65536 as 16 segments of 4096 chunks with h carried, fwd+bwd)
+# --------------------------------------------------------------------------------------
+SWEEP = [(4, 2, 2048), (4, 4, 2048), (4, 6, 2048), (4, 2, 4096), (4, 4, 4096), (4, 6, 4096), (1, 6, 65536)]
+# Published fwd+bwd latencies of the reference on TPU v5e-1 (README.md:26-31).
+PUBLISHED_FWDBWD_MS = {(4, 2, 2048): 1.701, (4, 2, 4096): 2.943, (4, 4, 2048): 2.702, (4, 4, 4096): 10.493,
+                       (4, 6, 2048): 2.888, (4, 6, 4096): 13.818}
+
+
+def run_sweep(args):
+    """One JSON line per (shape, pass).  Each timed step is bracketed by its own CUDA events and
+    preceded by an L2 flush (a 256 MB write outside the events), so shapes whose inputs fit in the
+    126 MB L2 are still timed from HBM."""
+    import atomic_gdn2
+    from atomic_gdn2 import make_blr_trainable, make_cfg
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    dtype = torch.float32 if args.dtype == "fp32" else torch.bfloat16
+    cfg = make_cfg(**CFG_KW)
+    if args.dtype == "bf16":
+        cfg = cfg.with_(dot_mode="default", solve_dot_mode="default", b3_dot_mode="default")
+    fn = make_blr_trainable(cfg, D ** -0.5)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    steps, warmup = max(1, min(args.steps, 20)), max(3, args.warmup)
+    for shape in SWEEP:
+        nb, nh, nl = shape
+        xs_base, h0 = make_inputs(7, dev, dtype, shape)
+        for mode in ("fwd", "fwd+bwd"):
+            if mode == "fwd":
+                xs = xs_base
+
+                def step():
+                    o, hf = fn(*xs, h0)
+                    return o
+            else:
+                xs = [t.detach().requires_grad_(True) for t in xs_base]
+
+                def step():
+                    o, hf = fn(*xs, h0)
+                    return torch.autograd.grad((o * o).sum() + (hf * hf).sum(), xs)
+            atomic_gdn2.set_checks(True)
+            step()
+            atomic_gdn2.set_checks(False)
+            for _ in range(warmup):
+                step()
+            times = []
+            for _ in range(steps):
+                flush.fill_(1)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                step()
+                e1.record()
+                torch.cuda.synchronize()
+                times.append(e0.elapsed_time(e1))
+            ms = statistics.median(times)
+            pub = PUBLISHED_FWDBWD_MS.get(shape) if mode == "fwd+bwd" else None
+            nchunk = nl // T
+            segs = math.ceil(nchunk / cfg.max_chunks_per_call)
+            line = {"sweep": True, "metric": f"GDN-2 {mode} tokens/s", "value": nb * nl / (ms / 1e3),
+                    "unit": "tokens/s", "ms_per_step": ms, "ms_min": min(times), "steps": steps, "warmup": warmup,
+                    "dtype": "f32" if dtype == torch.float32 else "bf16", "data": "synthetic",
+                    "config": {"workload": f"B{nb} H{nh} L{nl} D{D}", "segments": segs,
+                               "chunks_per_segment": min(nchunk, cfg.max_chunks_per_call),
+                               "l2": "flushed before every timed step"},
+                    "status": atomic_gdn2.last_status(),
+                    "tpu_v5e_published_ms": pub, "speedup_vs_published": (pub / ms) if pub else None}
+            print(json.dumps(line), flush=True)
+            del xs
+        del xs_base, h0
+        torch.cuda.empty_cache()
+
+
 def main():
     args = parse()
+    if args.sweep:
+        run_sweep(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:
