@@ -48,6 +48,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--dtype", default="fp32", choices=["fp32", "bf16"])
+    ap.add_argument("--workload", default="op", choices=["op", "lm"],
+                    help="op: the operator's fwd+bwd tokens/s (headline); lm: the 8-layer LM training step")
     ap.add_argument("--sweep", action="store_true",
                     help="instead of the headline line, print one line per sweep shape (BASELINE configs 3 and 4)")
     return ap.parse_args()
@@ -441,8 +443,137 @@ def run_sweep(args):
         torch.cuda.empty_cache()
 
 
+# --------------------------------------------------------------------------------------
+# LM step: 8-layer GDN-2 LM, B8 L2048 per GPU, data parallel over NCCL
+# --------------------------------------------------------------------------------------
+LM_B, LM_L = 8, 2048
+# The reference's published LM step (204.659 ms, TPU v5e-1, README.md:43) is for its notebook's
+# 34,873,952-parameter model, not this layer.py model (39,121,152 parameters): no vs_baseline.
+LM_PUBLISHED_MS_OTHER_MODEL = 204.659
+
+
+def run_lm(args):
+    import datetime
+    import atomic_gdn2
+    from atomic_gdn2 import _lib, make_cfg
+    from atomic_gdn2.training import GDN2LM, TrainStep, lm_config, make_optimizer
+    from atomic_gdn2.training.model import n_params
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.gpus != world:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    # dense layers in TF32 on the tensor cores (fp32 storage and accumulation)
+    torch.backends.cuda.matmul.allow_tf32 = True
+    cfg = make_cfg()
+    mc = lm_config()
+    model = GDN2LM(cfg, **mc, seed=0).to(dev)
+    net = model
+    if dist is not None:
+        from torch.nn.parallel import DistributedDataParallel as DDP
+        net = DDP(model, device_ids=[local], gradient_as_bucket_view=True, bucket_cap_mb=32)
+    opt = make_optimizer(model, 3e-4)
+    step = TrainStep(net, opt, lr=3e-4, warmup=200, total=2000)
+    gen = torch.Generator(device=dev).manual_seed(100 + rank)
+
+    def tokens():
+        return torch.randint(0, mc["vocab"], (LM_B, LM_L), generator=gen, device=dev)
+
+    atomic_gdn2.set_checks(True)
+    step(tokens())
+    atomic_gdn2.set_checks(False)
+    steps, warmup = max(1, min(args.steps, 20)), max(3, args.warmup)
+    batches = [tokens() for _ in range(steps)]
+    for _ in range(warmup):
+        step(batches[0])
+    clocks = Clocks(local)
+    clocks.start()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(steps):
+        loss, gn, ok = step(batches[i])
+    e1.record()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / steps
+    status = atomic_gdn2.last_status()
+
+    def max_over_ranks(x):
+        if dist is None:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    ms = max_over_ranks(ms)
+    # operator kernels inside one step
+    _lib.profile_enable(True)
+    step(batches[0])
+    torch.cuda.synchronize()
+    prof = _lib.profile_collect()
+    _lib.profile_enable(False)
+    # end to end: tokens from pinned host memory every step, loss read back every step
+    host = [b.cpu().pin_memory() for b in batches]
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for i in range(steps):
+        loss, gn, ok = step(host[i].to(dev, non_blocking=True))
+        lv = loss.item()
+    f1.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1) / steps)
+    final_loss = float(loss)
+    if rank == 0:
+        tok = world * LM_B * LM_L
+        op_ms = {n: round(t, 3) for n, (t, c) in prof.items() if c}
+        line = {
+            "metric": "GDN-2 LM step ms (8 layers, 39.1M params, B8 L2048 per GPU)", "value": ms, "unit": "ms",
+            "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": ms, "higher_is_better": False,
+            "scaling": "weak", "vs_baseline": None, "tokens_per_s": tok / (ms / 1e3), "dtype": "f32", "data":
+            "synthetic (uniform random byte tokens), random-init weights",
+            "config": {"workload": "LM training step: fwd, bwd, DP all-reduce, clip 1.0, AdamW lr 3e-4",
+                       "model": "atomic_gdn2 layer.py LM", "params": n_params(model), **mc,
+                       "global_batch": LM_B * world, "seq_len": LM_L, "parallelism": f"dp{world} (NCCL DDP)",
+                       "matmul": "tf32 tensor cores, fp32 storage", "operator_modes":
+                       {k: cfg.__dict__[k] for k in ("dot_mode", "solve_dot_mode", "b3_dot_mode")},
+                       "l2": "activations (~10 GB per step) exceed the 126 MB L2"},
+            "operator_kernels_ms_per_step": op_ms,
+            "operator_share": sum(op_ms.values()) / ms,
+            "e2e": {"value": e2e_ms, "unit": "ms", "h2d_bytes_per_step": LM_B * LM_L * 8, "d2h_bytes_per_step": 4},
+            "gpu_launches": 6 * len(model.layers) * steps,
+            "final_loss": final_loss,
+            "published_other_model_ms": LM_PUBLISHED_MS_OTHER_MODEL,
+            "clocks": clk, "device_status": status,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
+    if args.workload == "lm":
+        if args.impl == "reference":
+            if int(os.environ.get("RANK", "0")) == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "the reference LM step needs JAX/optax "
+                                  "(not installed); its CPU restatement is not timed at this size"}))
+            return
+        run_lm(args)
+        return
     if args.sweep:
         run_sweep(args)
         return

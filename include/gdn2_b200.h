@@ -142,6 +142,25 @@ gdn2_status gdn2_fwd_noalloc(const gdn2_desc* desc, const void* q, const void* k
                              const void* b, const void* g, const float* h0, float* o, float* h_final,
                              uint32_t* dev_status, void* stream);
 
+/*
+ * Fused layer prologue of the GDN-2 layer (atomic_gdn2/layer.py:31-40; the reference computes
+ * it as XLA-fused jnp code, so there is no single reference function this replaces).
+ * y is the layer's input projection, (B, L, 6, H, D) fp32 contiguous: the q, k, v, w, b, g
+ * projections side by side per token.  gdn2_prologue_fwd writes the operator inputs as six
+ * contiguous (B, H, L, D) fp32 tensors:
+ *   q, k = y_q, y_k L2-normalised over D (eps 1e-6) when l2norm != 0, else unchanged;
+ *   v, w = y_v, y_w;   b = sigmoid(y_b);   g = -min(softplus(y_g), g_max).
+ * gdn2_prologue_bwd takes y and the six (B, H, L, D) gradients and writes dy in y's layout
+ * (the activations are recomputed from y).  D must be 128 (GDN2_ERR_UNSUPPORTED otherwise);
+ * every pointer must be 16-byte aligned (GDN2_ERR_INVALID_ARGUMENT otherwise).
+ */
+gdn2_status gdn2_prologue_fwd(const float* y, int64_t B, int64_t L, int64_t H, int64_t D, float g_max,
+                              int32_t l2norm, float* q, float* k, float* v, float* w, float* b, float* g,
+                              void* stream);
+gdn2_status gdn2_prologue_bwd(const float* y, int64_t B, int64_t L, int64_t H, int64_t D, float g_max,
+                              int32_t l2norm, const float* dq, const float* dk, const float* dv, const float* dw,
+                              const float* db, const float* dg, float* dy, void* stream);
+
 /* Profiling hook (no counterpart in the reference).  While enabled, every kernel launch of
  * gdn2_fwd / gdn2_bwd is bracketed by CUDA events recorded on the caller's stream.
  * gdn2_profile_collect synchronises on those events, writes per-kernel summed milliseconds and
