@@ -50,6 +50,8 @@ def parse():
     ap.add_argument("--dtype", default="fp32", choices=["fp32", "bf16"])
     ap.add_argument("--workload", default="op", choices=["op", "lm"],
                     help="op: the operator's fwd+bwd tokens/s (headline); lm: the 8-layer LM training step")
+    ap.add_argument("--torch-profile", action="store_true",
+                    help="lm workload: also print torch.profiler's per-kernel CUDA time table for 2 steps")
     ap.add_argument("--sweep", action="store_true",
                     help="instead of the headline line, print one line per sweep shape (BASELINE configs 3 and 4)")
     return ap.parse_args()
@@ -536,6 +538,15 @@ def run_lm(args):
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(f0.elapsed_time(f1) / steps)
     final_loss = float(loss)
+    if args.torch_profile:      # every rank steps (the DDP all-reduce is collective); rank 0 prints
+        from torch.profiler import ProfilerActivity, profile
+        with profile(activities=[ProfilerActivity.CUDA]) as tp:
+            for i in range(2):
+                step(batches[i])
+            torch.cuda.synchronize()
+        if rank == 0:
+            print(tp.key_averages().table(sort_by="cuda_time_total", row_limit=40, max_name_column_width=70),
+                  file=sys.stderr, flush=True)
     if rank == 0:
         tok = world * LM_B * LM_L
         op_ms = {n: round(t, 3) for n, (t, c) in prof.items() if c}
