@@ -284,13 +284,20 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
 
   // 1. S0 = dv_new = sanitize(dvl + kg dh_next)                                  [B1, b3 mode]
   gemm1(m3, pool, mb, S0, kmaj(src_kg), mn_any(src_dhn), false, false);
-  for (int c0 = cb; c0 < cb + 64; c0 += 16) {
-    float x[16], y[16];
-    tmem_ld16(S0, c0, x);
-    ld16_f(dvl_g + t * kD + c0, y);
+  {
+    // global loads of the whole half-row first: the TMEM accesses below order all memory
+    // operations, so loads placed between them would each wait out a full latency
+    float y[64];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) x[j] = sanitize(x[j] + y[j], clip);
-    tmem_st16(S0, c0, x);
+    for (int j = 0; j < 4; ++j) ld16_f(dvl_g + t * kD + cb + 16 * j, y + 16 * j);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float x[16];
+      tmem_ld16(S0, cb + 16 * j, x);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) x[i] = sanitize(x[i] + y[16 * j + i], clip);
+      tmem_st16(S0, cb + 16 * j, x);
+    }
   }
   sync_all();
   // 2. S1 = dwp' = -dv_new (e^m h_pre)^T                                          [B3]
@@ -308,17 +315,27 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
   sync_all();
   // 4. S3 = dwv = A^T dv_new;  dw = dwv v, dv = dwv w                              [B3]
   gemm1(m3, pool, mb, S3, mn_any(src_ainv), mn_own(tm(S0)), false, false);
-  for (int c0 = cb; c0 < cb + 64; c0 += 16) {
-    float x[16], a[16], y[16];
-    tmem_ld16(S3, c0, x);
-    ld16_in(v + t * kD + c0, a);
+  {
+    float* xb = xbuf(sm);
+    tmem_to_xbuf(S3, cb, xb);
+    const int r0 = (warp & 3) * 32;
+#pragma unroll 8
+    for (int i = 0; i < 16; ++i) {
+      const int lr = xrow(i), c0 = cb + xcol();
+      const float4 d4 = *reinterpret_cast<const float4*>(xb + lr * kXPitch + xcol());
+      const float d[4] = {d4.x, d4.y, d4.z, d4.w};
+      float vv[4], ww[4], y[4], z[4];
+      ld4(v + (r0 + lr) * kD + c0, vv);
+      ld4(w + (r0 + lr) * kD + c0, ww);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) y[j] = sanitize(x[j] * a[j], clip);
-    st16_out(dw + t * kD + c0, y);
-    ld16_in(w + t * kD + c0, a);
-#pragma unroll
-    for (int j = 0; j < 16; ++j) y[j] = sanitize(x[j] * a[j], clip);
-    st16_out(dv + t * kD + c0, y);
+      for (int e = 0; e < 4; ++e) {
+        y[e] = sanitize(d[e] * vv[e], clip);
+        z[e] = sanitize(d[e] * ww[e], clip);
+      }
+      st4(dw + (r0 + lr) * kD + c0, y);
+      st4(dv + (r0 + lr) * kD + c0, z);
+    }
+    __syncthreads();  // the buffers live in the operand pool the next product stages into
   }
   // 5. S0 = tmp = sanitize(dA A^T)                                                   [B3]
   gemm1(m3, pool, mb, S0, kmaj(tm(S2)), kmaj(src_ainv), false, false);
@@ -362,32 +379,44 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
   // 10.-11. finish dq and db;  S3 <- dgc partial;  S0 <- Dbk b E (pre-scaled dk partial)
   {
     const float* gr = gcrow(t);
-    for (int c0 = cb; c0 < cb + 64; c0 += 16) {
-      float x[16], y[16], qv[16], kv[16], bv[16], E[16], dgcp[16];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) E[j] = ex(gr[c0 + j] - mid_s[c0 + j]);
-      ld16_in(q + t * kD + c0, qv);
-      ld16_in(k + t * kD + c0, kv);
-      ld16_in(b + t * kD + c0, bv);
-      tmem_ld16(S3, c0, x);  // Dq / E
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        x[j] *= E[j];
-        y[j] = sanitize(x[j], clip);
-        dgcp[j] = qv[j] * x[j];
+#pragma unroll 1
+    for (int hh = 0; hh < 2; ++hh) {
+      float q2[32], k2[32], b2[32];
+  #pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        ld16_in(q + t * kD + cb + 32 * hh + 16 * j, q2 + 16 * j);
+        ld16_in(k + t * kD + cb + 32 * hh + 16 * j, k2 + 16 * j);
+        ld16_in(b + t * kD + cb + 32 * hh + 16 * j, b2 + 16 * j);
       }
-      st16_out(dq + t * kD + c0, y);
-      tmem_ld16(S0, c0, x);  // Dbk / E
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        x[j] *= E[j];
-        y[j] = sanitize(x[j] * kv[j], clip);
-        dgcp[j] += 2.f * bv[j] * kv[j] * x[j];
-        x[j] = x[j] * bv[j] * E[j];
+  #pragma unroll
+      for (int jj = 0; jj < 2; ++jj) {
+        const int c0 = cb + 32 * hh + 16 * jj;
+        const float* qv = q2 + 16 * jj;
+        const float* kv = k2 + 16 * jj;
+        const float* bv = b2 + 16 * jj;
+        float x[16], y[16], E[16], dgcp[16];
+  #pragma unroll
+        for (int j = 0; j < 16; ++j) E[j] = ex(gr[c0 + j] - mid_s[c0 + j]);
+        tmem_ld16(S3, c0, x);  // Dq / E
+  #pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          x[j] *= E[j];
+          y[j] = sanitize(x[j], clip);
+          dgcp[j] = qv[j] * x[j];
+        }
+        st16_out(dq + t * kD + c0, y);
+        tmem_ld16(S0, c0, x);  // Dbk / E
+  #pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          x[j] *= E[j];
+          y[j] = sanitize(x[j] * kv[j], clip);
+          dgcp[j] += 2.f * bv[j] * kv[j] * x[j];
+          x[j] = x[j] * bv[j] * E[j];
+        }
+        st16_out(db + t * kD + c0, y);
+        tmem_st16(S3, c0, dgcp);
+        tmem_st16(S0, c0, x);
       }
-      st16_out(db + t * kD + c0, y);
-      tmem_st16(S3, c0, dgcp);
-      tmem_st16(S0, c0, x);
     }
   }
   sync_all();
@@ -399,9 +428,14 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
   //     thread's own half-row of gcs (no other thread reads that row any more).
   {
     float* gr = gcs + t * kGcPitch;
-    for (int c0 = cb; c0 < cb + 64; c0 += 16) {
-      float x[16], y[16], kv[16], dgcp[16];
-      ld16_in(k + t * kD + c0, kv);
+    float k4[64];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) ld16_in(k + t * kD + cb + 16 * j, k4 + 16 * j);
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+      const int c0 = cb + 16 * jj;
+      const float* kv = k4 + 16 * jj;
+      float x[16], y[16], dgcp[16];
       tmem_ld16(S0, c0, x);
       tmem_ld16(S3, c0, dgcp);
 #pragma unroll

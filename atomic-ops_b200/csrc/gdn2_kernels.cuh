@@ -413,6 +413,34 @@ __device__ __forceinline__ void gemm2(Mode m, uint32_t pool, MmaBar& mb, uint32_
   }
 }
 
+// ---------------------------------------------------------------------------
+// Coalesced epilogues.  A thread's TMEM row (its lane) maps to one global row, so row-per-thread
+// global accesses make every warp-wide 16-byte access touch 32 rows.  These helpers move a warp's
+// 32 x 64 quarter of an accumulator through a warp-private buffer in the idle operand pool, after
+// which lane l handles 4 consecutive columns of two rows per step (rows 2i + l / 16): each
+// warp-wide access then covers two contiguous 256-byte row segments.
+// ---------------------------------------------------------------------------
+constexpr int kXPitch = 68;  // floats per buffered row (64 + 4: conflict-free 16-byte accesses)
+__device__ __forceinline__ float* xbuf(uint8_t* pool_base) {
+  return reinterpret_cast<float*>(pool_base) + (threadIdx.x >> 5) * 32 * kXPitch;
+}
+// This thread's 64-column half-row [cb, cb + 64) of TMEM slot `slot` -> the warp's buffer, row = lane.
+__device__ __forceinline__ void tmem_to_xbuf(uint32_t slot, int cb, float* xb) {
+  float* row = xb + (threadIdx.x & 31) * kXPitch;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float x[16];
+    tmem_ld16(slot, (uint32_t)(cb + 16 * j), x);
+#pragma unroll
+    for (int i = 0; i < 16; i += 4)
+      *reinterpret_cast<float4*>(row + 16 * j + i) = make_float4(x[i], x[i + 1], x[i + 2], x[i + 3]);
+  }
+  __syncwarp();
+}
+// Coalesced position of step i (0..15): the warp-local row (0..31) and column offset (0..60).
+__device__ __forceinline__ int xrow(int i) { return 2 * i + ((threadIdx.x & 31) >> 4); }
+__device__ __forceinline__ int xcol() { return 4 * (threadIdx.x & 15); }
+
 // Row loaders (16 values)
 template <class TIn>
 __device__ __forceinline__ void ld16_in(const TIn* p, float* x) {
