@@ -7,8 +7,13 @@ place of jax.custom_vjp:
   ValueError (pipeline.py:54-55); h0 is (B, H, D, D) fp32 or None for zeros (pipeline.py:57);
 * o and h_final are fp32 (pipeline.py:45 returns the f32 kernel output);
 * long sequences are processed in segments of cfg.max_chunks_per_call chunks that carry h
-  (pipeline.py:59-64); the whole call is one autograd node, the per-segment launches write into
-  strided views of one output, so there is no concatenation copy;
+  (pipeline.py:59-64); the whole call is one autograd node, the launches write into strided views
+  of one output, so there is no concatenation copy.  Consecutive segments run as one launch
+  sequence (the scans carry h and dh across the segment boundaries on the device) as long as the
+  group's transient backward workspace stays under GDN2_SEGMENT_GROUP_BYTES (default 4 GiB); the
+  result is bit-identical to one launch sequence per segment, because the scans store and reload
+  the carried state unchanged at a boundary and every other kernel is chunk-local.  Residuals
+  are the same size either way (the reference also keeps every segment's residuals);
 * backward returns gradients for all seven arguments, each in its input's dtype after the final
   sanitize at 1e4 (pipeline.py:11-14, 38-47); do and dh_final are taken as fp32 (pipeline.py:42).
 
@@ -27,6 +32,17 @@ from .config import BLRConfig
 
 _FINAL_CLIP = 1e4
 _checks = os.environ.get("GDN2_CHECK", "1") != "0"
+_group_bytes = int(os.environ.get("GDN2_SEGMENT_GROUP_BYTES", str(4 << 30)))
+
+
+def _segment_groups(lib, cfg, scale, B, H, D, sb, sh, dtype, nc):
+    """Chunk ranges [s, e) of the launches: whole segments of cfg.max_chunks_per_call chunks,
+    grouped while the group's backward workspace fits the byte budget (at least one segment)."""
+    seg = cfg.max_chunks_per_call
+    one = _make_desc(cfg, scale, B, H, min(nc, seg) * cfg.bt, D, sb, sh, dtype)
+    ws_seg = max(1, lib.gdn2_bwd_workspace_bytes(ctypes.byref(one)))
+    per_group = max(1, _group_bytes // ws_seg) * seg
+    return [(s, min(nc, s + per_group)) for s in range(0, nc, per_group)]
 
 
 def set_checks(enabled: bool) -> None:
@@ -103,7 +119,6 @@ class _GDN2(torch.autograd.Function):
         B, H, L, D = q.shape
         dev = q.device
         nc = L // cfg.bt
-        seg = cfg.max_chunks_per_call
         # o shares the inputs' (b, h) strides: the C ABI addresses every (B,H,L,D) tensor of a call
         # with one stride pair (views of longer sequences are consumed without copies)
         o = torch.empty_strided((B, H, L, D), q.stride(), dtype=torch.float32, device=dev)
@@ -116,8 +131,7 @@ class _GDN2(torch.autograd.Function):
             sb = max(sb, H * sh)
         h = h0
         segments, residuals = [], []
-        for s in range(0, nc, seg):
-            e = min(nc, s + seg)
+        for s, e in _segment_groups(lib, cfg, scale, B, H, D, sb, sh, q.dtype, nc):
             a = s * cfg.bt
             desc = _make_desc(cfg, scale, B, H, (e - s) * cfg.bt, D, sb, sh, q.dtype)
             nbytes = lib.gdn2_residual_bytes(ctypes.byref(desc))

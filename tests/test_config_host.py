@@ -143,3 +143,20 @@ def test_domain_stats():
     assert domain.safe_bs2_for(5.0) == 16
     mx, mean = domain.bk2_stat(torch.ones(2, 4), torch.full((2, 4), 0.5))
     assert mx == 2.0 and mean == 2.0
+
+
+def test_segment_groups_cover_the_sequence(monkeypatch):
+    """Launch groups are whole segments, cover every chunk once, and respect the byte budget."""
+    from atomic_gdn2 import pipeline
+    lib = _lib.load()
+    cfg = make_cfg(max_chunks_per_call=32)
+    args = (lib, cfg, 0.1, 1, 6, 128, 6 * 65536 * 128, 65536 * 128, torch.float32, 512)
+    assert pipeline._segment_groups(*args) == [(0, 512)]          # 16 segments, one launch sequence
+    monkeypatch.setattr(pipeline, "_group_bytes", 1)
+    g = pipeline._segment_groups(*args)
+    assert g == [(s, s + 32) for s in range(0, 512, 32)]
+    one = pipeline._make_desc(cfg, 0.1, 1, 6, 32 * 128, 128, 6 * 65536 * 128, 65536 * 128, torch.float32)
+    ws = lib.gdn2_bwd_workspace_bytes(ctypes.byref(one))
+    monkeypatch.setattr(pipeline, "_group_bytes", 3 * ws + 1)
+    g = pipeline._segment_groups(*args)
+    assert g[0] == (0, 96) and g[-1][1] == 512 and all(b == c for (_, b), (c, _) in zip(g, g[1:]))

@@ -136,6 +136,21 @@ def test_segmentation_is_exact():
         assert torch.equal(x, y) and torch.equal(x, z)
 
 
+def test_segment_grouping_is_exact(monkeypatch):
+    """Segments grouped into one launch sequence (h and dh carried by the scans) against one launch
+    sequence per segment (h_final -> h0 and dh0 -> dh_final through memory): bit for bit."""
+    from atomic_gdn2 import pipeline
+    cfg = make_cfg(max_chunks_per_call=2)
+    xs, h0 = O.bench_inputs(1, 2, 1024, D, 5)
+    grouped = _run_op(cfg, xs, h0)
+    monkeypatch.setattr(pipeline, "_group_bytes", 1)      # every group is a single segment
+    assert len(pipeline._segment_groups(pipeline._lib.load(), cfg, 0.1, 1, 2, D, 2 * 1024 * D, 1024 * D,
+                                        torch.float32, 8)) == 4
+    per_segment = _run_op(cfg, xs, h0)
+    for x, y in zip(grouped, per_segment):
+        assert torch.equal(x, y)
+
+
 def test_determinism():
     cfg = make_cfg()
     xs, h0 = O.bench_inputs(1, 3, 256, D, 4)
