@@ -82,22 +82,23 @@ __global__ void __launch_bounds__(kCT, 1) bwd_pre_kernel(const BwdParams P) {
   const uint32_t S0 = tb, S1 = tb + 128;
   MmaBar mb{bar, 0u, p.status};
 
-  auto src_aqk = [&](int r, int c0, float* x) { ld16_f(aqk_g + r * kT + c0, x); };
-  auto src_do = [&](int r, int c0, float* x) { ld16_f(do_ + r * kD + c0, x); };
+  // global row sources: 4 values of row r from column c0 (mn_any operands)
+  auto src_aqk = [&](int r, int c0, float* x) { ld4_f(aqk_g + r * kT + c0, x); };
+  auto src_do = [&](int r, int c0, float* x) { ld4_f(do_ + r * kD + c0, x); };
   auto src_qg = [&](int r, int c0, float* x) {
-    ld16_in(q + r * kD + c0, x);
+    ld4_in(q + r * kD + c0, x);
     const float* gr = gcs + r * kGcPitch + c0;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) x[j] = scale * sanitize(x[j] * ex(fminf(gr[j], 0.f)), clip);
+    for (int j = 0; j < 4; ++j) x[j] = scale * sanitize(x[j] * ex(fminf(gr[j], 0.f)), clip);
   };
   auto src_kg = [&](int r, int c0, float* x) {  // sanitize(k e^min(gl - gc, 0))
-    ld16_in(k + r * kD + c0, x);
+    ld4_in(k + r * kD + c0, x);
     const float* gr = gcs + r * kGcPitch + c0;
     const float* gl = gcs + (kT - 1) * kGcPitch + c0;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) x[j] = sanitize(x[j] * ex(fminf(gl[j] - gr[j], 0.f)), clip);
+    for (int j = 0; j < 4; ++j) x[j] = sanitize(x[j] * ex(fminf(gl[j] - gr[j], 0.f)), clip);
   };
-  auto src_wp = [&](int r, int c0, float* x) { ld16_f(wp_g + r * kD + c0, x); };
+  auto src_wp = [&](int r, int c0, float* x) { ld4_f(wp_g + r * kD + c0, x); };
   auto tm0 = [&](int, int c0, float* x) { tmem_ld16(S0, (uint32_t)c0, x); };
 
   // S0 = Aqk^T do, S1 = (scale qg)^T do   (shared B = do)
@@ -217,61 +218,61 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
     tc_fence_after();
   };
 
-  // ---- row sources: 16 values of row r from column c0 ----
+  // ---- global row sources: 4 values of row r from column c0 (kany / mn_any operands) ----
   auto gcrow = [&](int r) { return gcs + r * kGcPitch; };
   auto src_kg = [&](int r, int c0, float* x) {
-    ld16_in(k + r * kD + c0, x);
+    ld4_in(k + r * kD + c0, x);
     const float* gr = gcrow(r) + c0;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) x[j] = sanitize(x[j] * ex(fminf(gl_s[c0 + j] - gr[j], 0.f)), clip);
+    for (int j = 0; j < 4; ++j) x[j] = sanitize(x[j] * ex(fminf(gl_s[c0 + j] - gr[j], 0.f)), clip);
   };
-  auto src_dhn = [&](int r, int c0, float* x) { ld16_f(dhn_g + r * kD + c0, x); };
+  auto src_dhn = [&](int r, int c0, float* x) { ld4_f(dhn_g + r * kD + c0, x); };
   auto src_hpre_em = [&](int r, int c0, float* x) {  // row d = r of e^m h_pre
-    ld16_f(hpre_g + r * kD + c0, x);
+    ld4_f(hpre_g + r * kD + c0, x);
     const float s = ex(mid_s[r]);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) x[j] *= s;
+    for (int j = 0; j < 4; ++j) x[j] *= s;
   };
   auto src_dhn_gl = [&](int r, int c0, float* x) {  // row d = r of e^(gl-m) dh_next
-    ld16_f(dhn_g + r * kD + c0, x);
+    ld4_f(dhn_g + r * kD + c0, x);
     const float s = ex(gl_s[r] - mid_s[r]);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) x[j] *= s;
+    for (int j = 0; j < 4; ++j) x[j] *= s;
   };
   auto src_bkE = [&](int r, int c0, float* x) {
-    float kv[16];
-    ld16_in(b + r * kD + c0, x);
-    ld16_in(k + r * kD + c0, kv);
+    float kv[4];
+    ld4_in(b + r * kD + c0, x);
+    ld4_in(k + r * kD + c0, kv);
     const float* gr = gcrow(r) + c0;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) x[j] = x[j] * kv[j] * ex(gr[j] - mid_s[c0 + j]);
+    for (int j = 0; j < 4; ++j) x[j] = x[j] * kv[j] * ex(gr[j] - mid_s[c0 + j]);
   };
   auto src_qE = [&](int r, int c0, float* x) {
-    ld16_in(q + r * kD + c0, x);
+    ld4_in(q + r * kD + c0, x);
     const float* gr = gcrow(r) + c0;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) x[j] = scale * x[j] * ex(gr[j] - mid_s[c0 + j]);
+    for (int j = 0; j < 4; ++j) x[j] = scale * x[j] * ex(gr[j] - mid_s[c0 + j]);
   };
   auto src_kF = [&](int r, int c0, float* x) {
-    ld16_in(k + r * kD + c0, x);
+    ld4_in(k + r * kD + c0, x);
     const float* gr = gcrow(r) + c0;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) x[j] = x[j] * ex(mid_s[c0 + j] - gr[j]);
+    for (int j = 0; j < 4; ++j) x[j] = x[j] * ex(mid_s[c0 + j] - gr[j]);
   };
   auto src_wv = [&](int r, int c0, float* x) {
-    float vv[16];
-    ld16_in(w + r * kD + c0, x);
-    ld16_in(v + r * kD + c0, vv);
+    float vv[4];
+    ld4_in(w + r * kD + c0, x);
+    ld4_in(v + r * kD + c0, vv);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) x[j] *= vv[j];
+    for (int j = 0; j < 4; ++j) x[j] *= vv[j];
   };
-  auto src_ainv = [&](int r, int c0, float* x) { ld16_f(ainv_g + r * kT + c0, x); };
-  auto src_vnew = [&](int r, int c0, float* x) { ld16_f(vnew_g + r * kD + c0, x); };
-  auto src_do = [&](int r, int c0, float* x) { ld16_f(do_ + r * kD + c0, x); };
+  auto src_ainv = [&](int r, int c0, float* x) { ld4_f(ainv_g + r * kT + c0, x); };
+  auto src_vnew = [&](int r, int c0, float* x) { ld4_f(vnew_g + r * kD + c0, x); };
+  auto src_do = [&](int r, int c0, float* x) { ld4_f(do_ + r * kD + c0, x); };
   auto src_do_s = [&](int r, int c0, float* x) {
-    ld16_f(do_ + r * kD + c0, x);
+    ld4_f(do_ + r * kD + c0, x);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) x[j] *= scale;
+    for (int j = 0; j < 4; ++j) x[j] *= scale;
   };
   auto tm = [&](uint32_t slot) { return [=](int, int c0, float* x) { tmem_ld16(slot, (uint32_t)c0, x); }; };
   auto tm_scaled = [&](uint32_t slot) {
@@ -283,7 +284,7 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
   };
 
   // 1. S0 = dv_new = sanitize(dvl + kg dh_next)                                  [B1, b3 mode]
-  gemm1(m3, pool, mb, S0, kmaj(src_kg), mn_any(src_dhn), false, false);
+  gemm1(m3, pool, mb, S0, kany(src_kg), mn_any(src_dhn), false, false);
   {
     // global loads of the whole half-row first: the TMEM accesses below order all memory
     // operations, so loads placed between them would each wait out a full latency
@@ -301,9 +302,9 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
   }
   sync_all();
   // 2. S1 = dwp' = -dv_new (e^m h_pre)^T                                          [B3]
-  gemm1(m3, pool, mb, S1, kmaj(tm(S0)), kmaj(src_hpre_em), true, false);
+  gemm1(m3, pool, mb, S1, kmaj(tm(S0)), kany(src_hpre_em), true, false);
   // 3. S2 = dA = sanitize(dwp' (bk E)^T + dv_new (w v)^T)                          [B3]
-  gemm2(m3, pool, mb, S2, kmaj(tm(S1)), kmaj(src_bkE), false, false, S2, kmaj(tm(S0)), kmaj(src_wv), false, true,
+  gemm2(m3, pool, mb, S2, kmaj(tm(S1)), kany(src_bkE), false, false, S2, kmaj(tm(S0)), kany(src_wv), false, true,
         false, false);
   for (int c0 = cb; c0 < cb + 64; c0 += 16) {
     float x[16];
@@ -338,7 +339,7 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
     __syncthreads();  // the buffers live in the operand pool the next product stages into
   }
   // 5. S0 = tmp = sanitize(dA A^T)                                                   [B3]
-  gemm1(m3, pool, mb, S0, kmaj(tm(S2)), kmaj(src_ainv), false, false);
+  gemm1(m3, pool, mb, S0, kmaj(tm(S2)), kany(src_ainv), false, false);
   for (int c0 = cb; c0 < cb + 64; c0 += 16) {
     float x[16];
     tmem_ld16(S0, c0, x);
@@ -364,7 +365,7 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
   gemm1(m3, pool, mb, S0, mn_any(src_ainv), mn_own(tm(S1)), false, false);
   gemm1(mh, pool, mb, S0, kmaj(tm(S2)), mn_any(src_kF), false, true);
   // 8. S1 = dAqk = (do v_new^T) causal                                              [B2]
-  gemm1(m3, pool, mb, S1, kmaj(src_do), kmaj(src_vnew), false, false);
+  gemm1(m3, pool, mb, S1, kany(src_do), kany(src_vnew), false, false);
   for (int c0 = cb; c0 < cb + 64; c0 += 16) {
     float x[16];
     tmem_ld16(S1, c0, x);
@@ -374,7 +375,7 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
   }
   sync_all();
   // 9. S3 = scale do (e^m h_pre)^T (B3)  +  scale dAqk (k F) (B4)
-  gemm1(m3, pool, mb, S3, kmaj(src_do_s), kmaj(src_hpre_em), false, false);
+  gemm1(m3, pool, mb, S3, kany(src_do_s), kany(src_hpre_em), false, false);
   gemm1(mh, pool, mb, S3, kmaj(tm_scaled(S1)), mn_any(src_kF), false, true);
   // 10.-11. finish dq and db;  S3 <- dgc partial;  S0 <- Dbk b E (pre-scaled dk partial)
   {
@@ -421,7 +422,7 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
   }
   sync_all();
   // 12. S0 += v_new (e^(gl-m) dh_next)^T (B3)  +  scale dAqk^T (q E) + dAkk^T (bk E) (B4)
-  gemm1(m3, pool, mb, S0, kmaj(src_vnew), kmaj(src_dhn_gl), false, true);
+  gemm1(m3, pool, mb, S0, kany(src_vnew), kany(src_dhn_gl), false, true);
   gemm2(mh, pool, mb, S0, mn_own(tm(S1)), mn_any(src_qE), false, true, S0, mn_own(tm(S2)), mn_any(src_bkE), false,
         true, false, false);
   // 13. dk = F o S0;  dgc = S3 - k o dk (+ decay term on the last row).  dgc overwrites this

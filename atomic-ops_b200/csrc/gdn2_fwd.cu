@@ -103,48 +103,49 @@ __global__ void __launch_bounds__(kCT, 1) fwd_intra_kernel(const OpParams p) {
   MmaBar mbar{bar, 0u, p.status};
   __syncthreads();
 
-  // ---- row sources: 16 values of row r from column c0 (global / smem ones for any row) -------
+  // ---- global row sources (4 values of row r from column c0: kany / mn_any operands) -----------
   auto src_qE = [&](int r, int c0, float* x) {  // q e^(gc - m)
-    ld16_in(q + r * kD + c0, x);
+    ld4_in(q + r * kD + c0, x);
     const float* gr = gcs + r * kGcPitch + c0;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) x[j] *= ex(gr[j] - mid_s[c0 + j]);
+    for (int j = 0; j < 4; ++j) x[j] *= ex(gr[j] - mid_s[c0 + j]);
   };
   auto src_bkE = [&](int r, int c0, float* x) {  // b k e^(gc - m)
-    float kv[16];
-    ld16_in(b + r * kD + c0, x);
-    ld16_in(k + r * kD + c0, kv);
+    float kv[4];
+    ld4_in(b + r * kD + c0, x);
+    ld4_in(k + r * kD + c0, kv);
     const float* gr = gcs + r * kGcPitch + c0;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) x[j] = x[j] * kv[j] * ex(gr[j] - mid_s[c0 + j]);
+    for (int j = 0; j < 4; ++j) x[j] = x[j] * kv[j] * ex(gr[j] - mid_s[c0 + j]);
   };
   auto src_kF = [&](int r, int c0, float* x) {  // k e^(m - gc)
-    ld16_in(k + r * kD + c0, x);
+    ld4_in(k + r * kD + c0, x);
     const float* gr = gcs + r * kGcPitch + c0;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) x[j] *= ex(mid_s[c0 + j] - gr[j]);
+    for (int j = 0; j < 4; ++j) x[j] *= ex(mid_s[c0 + j] - gr[j]);
   };
   auto src_kb = [&](int r, int c0, float* x) {  // b k e^min(gc, 0)
-    float kv[16];
-    ld16_in(b + r * kD + c0, x);
-    ld16_in(k + r * kD + c0, kv);
+    float kv[4];
+    ld4_in(b + r * kD + c0, x);
+    ld4_in(k + r * kD + c0, kv);
     const float* gr = gcs + r * kGcPitch + c0;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) x[j] = x[j] * kv[j] * ex(fminf(gr[j], 0.f));
+    for (int j = 0; j < 4; ++j) x[j] = x[j] * kv[j] * ex(fminf(gr[j], 0.f));
   };
   auto src_wv = [&](int r, int c0, float* x) {
-    float vv[16];
-    ld16_in(w + r * kD + c0, x);
-    ld16_in(v + r * kD + c0, vv);
+    float vv[4];
+    ld4_in(w + r * kD + c0, x);
+    ld4_in(v + r * kD + c0, vv);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) x[j] *= vv[j];
+    for (int j = 0; j < 4; ++j) x[j] *= vv[j];
   };
   auto src_kg = [&](int r, int c0, float* x) {  // sanitize(k e^min(gl - gc, 0))
-    ld16_in(k + r * kD + c0, x);
+    ld4_in(k + r * kD + c0, x);
     const float* gr = gcs + r * kGcPitch + c0;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) x[j] = sanitize(x[j] * ex(fminf(gl_s[c0 + j] - gr[j], 0.f)), clip);
+    for (int j = 0; j < 4; ++j) x[j] = sanitize(x[j] * ex(fminf(gl_s[c0 + j] - gr[j], 0.f)), clip);
   };
+  // ---- shared-memory / TMEM row sources (16 values: kmaj / mn_own operands) ---------------------
   auto src_dinv = [&](int r, int c0, float* x) {  // row r of the block-diagonal Dg^-1
     if ((c0 >> 5) == (r >> 5)) {
       const float* src = dsm + (r >> 5) * 1056 + (r & 31) * 33 + (c0 & 31);
@@ -161,10 +162,16 @@ __global__ void __launch_bounds__(kCT, 1) fwd_intra_kernel(const OpParams p) {
 #pragma unroll
     for (int j = 0; j < 16; ++j) x[j] = (c0 + j < lim) ? x[j] : 0.f;
   };
+  auto src_dinv4 = [&](int r, int c0, float* x) {  // 4 values of row r of Dg^-1 (mn_any operand)
+    const bool in = (c0 >> 5) == (r >> 5);
+    const float* src = dsm + (r >> 5) * 1056 + (r & 31) * 33 + (c0 & 31);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) x[j] = in ? src[j] : 0.f;
+  };
   auto tm = [&](uint32_t slot) { return [=](int, int c0, float* x) { tmem_ld16(slot, (uint32_t)c0, x); }; };
 
   // ---- 1. scores: S0 = (q E)(k F)^T, S1 = (b k E)(k F)^T                      (dot mode) --------
-  gemm2(md, pool, mbar, S0, kmaj(src_qE), kmaj(src_kF), false, false, S1, kmaj(src_bkE), kmaj(NoSrc()), false,
+  gemm2(md, pool, mbar, S0, kany(src_qE), kany(src_kF), false, false, S1, kany(src_bkE), kany(NoSrc()), false,
         false, false, true);
 
   // ---- 2. Aqk out (scale, causal, sanitize); Se = (1-eps) sanitize(Akk) strict, in place -----------
@@ -211,7 +218,7 @@ __global__ void __launch_bounds__(kCT, 1) fwd_intra_kernel(const OpParams p) {
   // ---- 4.-7. A = (I - W)(I + W^2) Dg^-1,  W = Dg^-1 R                          (solve mode) --------
   gemm1(ms, pool, mbar, S0, kmaj(src_dinv), mn_own(src_R), false, false);   // W -> S0
   gemm1(ms, pool, mbar, S2, kmaj(tm(S0)), mn_own(tm(S0)), false, false);    // W^2 -> S2
-  gemm1(ms, pool, mbar, S3, kmaj(tm(S2)), mn_any(src_dinv), false, false);  // W^2 Dg^-1 -> S3
+  gemm1(ms, pool, mbar, S3, kmaj(tm(S2)), mn_any(src_dinv4), false, false);  // W^2 Dg^-1 -> S3
   for (int c0 = cb; c0 < cb + 64; c0 += 16) {                               // P = S3 + Dg^-1
     float x[16], dv[16];
     tmem_ld16(S3, c0, x);
@@ -327,19 +334,20 @@ __global__ void __launch_bounds__(kCT, 1) fwd_out_kernel(const OpParams p, float
   const uint32_t S0 = tb, S1 = tb + 128;
   MmaBar mbar{bar, 0u, p.status};
 
-  auto src_wp = [&](int r, int c0, float* x) { ld16_f(wp_g + r * kD + c0, x); };
+  // global row sources: 4 values of row r from column c0 (kany / mn_any operands)
+  auto src_wp = [&](int r, int c0, float* x) { ld4_f(wp_g + r * kD + c0, x); };
   auto src_qg = [&](int r, int c0, float* x) {  // scale sanitize(q e^min(gc, 0))
-    ld16_in(q + r * kD + c0, x);
+    ld4_in(q + r * kD + c0, x);
     const float* gr = gcs + r * kGcPitch + c0;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) x[j] = scale * sanitize(x[j] * ex(fminf(gr[j], 0.f)), clip);
+    for (int j = 0; j < 4; ++j) x[j] = scale * sanitize(x[j] * ex(fminf(gr[j], 0.f)), clip);
   };
-  auto src_h = [&](int r, int c0, float* x) { ld16_f(h_g + r * kD + c0, x); };
-  auto src_aqk = [&](int r, int c0, float* x) { ld16_f(aqk_g + r * kT + c0, x); };
+  auto src_h = [&](int r, int c0, float* x) { ld4_f(h_g + r * kD + c0, x); };
+  auto src_aqk = [&](int r, int c0, float* x) { ld4_f(aqk_g + r * kT + c0, x); };
   auto tm0 = [&](int, int c0, float* x) { tmem_ld16(S0, (uint32_t)c0, x); };
 
   // S0 = wp h_pre,  S1 = (scale qg) h_pre   (shared B = h_pre)
-  gemm2(md, pool, mbar, S0, kmaj(src_wp), mn_any(src_h), false, false, S1, kmaj(src_qg), mn_any(NoSrc()), false,
+  gemm2(md, pool, mbar, S0, kany(src_wp), mn_any(src_h), false, false, S1, kany(src_qg), mn_any(NoSrc()), false,
         false, false, true);
   // v_new = u - S0 (kept in S0 and written as a residual)
   for (int c0 = cb; c0 < cb + 64; c0 += 16) {
@@ -355,7 +363,7 @@ __global__ void __launch_bounds__(kCT, 1) fwd_out_kernel(const OpParams p, float
   __syncthreads();
   tc_fence_after();
   // S1 += Aqk v_new
-  gemm1(md, pool, mbar, S1, kmaj(src_aqk), mn_own(tm0), false, true);
+  gemm1(md, pool, mbar, S1, kany(src_aqk), mn_own(tm0), false, true);
   for (int c0 = cb; c0 < cb + 64; c0 += 16) {
     float x[16];
     tmem_ld16(S1, c0, x);

@@ -104,10 +104,17 @@ struct MmaBar {
 __device__ __forceinline__ int esize(Mode m) { return m.fmt == kTF32 ? 4 : 2; }
 __device__ __forceinline__ int kslice(Mode m) { return m.fmt == kTF32 ? 32 : 64; }
 
-// Operand pool: tile i is 16 KB at base + i * 16 KB.
-__device__ __forceinline__ Tile pool_k(uint32_t base, int i) { return tile_k(base + (uint32_t)i * 16384u, 128); }
+// Operand pool: tile i is 16 KB at base + i * 16 KB (1024-byte aligned), swizzled layouts (see the
+// staging engine below).  K-major: SWIZZLE_128B, SBO = 1024 (8 rows), one MMA K-step = 32 bytes.
+// MN-major bf16: SWIZZLE_128B, LBO = 1024 (next 64 MN), SBO = 2048 (next 8 k), K-step = 16 k.
+// MN-major tf32: SWIZZLE_128B_BASE32B (tile_mn).
+__device__ __forceinline__ Tile pool_k(uint32_t base, int i) {
+  return Tile{base + (uint32_t)i * 16384u, 16u, 1024u, 32u, false, 2u};
+}
 __device__ __forceinline__ Tile pool_mn(uint32_t base, int i, Mode m) {
-  return tile_mn(base + (uint32_t)i * 16384u, 128u * (uint32_t)esize(m), m.fmt);
+  const uint32_t a = base + (uint32_t)i * 16384u;
+  if (m.fmt == kTF32) return tile_mn(a, 512u, kTF32);
+  return Tile{a, 1024u, 2048u, 4096u, true, 2u};
 }
 
 // Issue one K-slice (4 MMA K-steps) for operand pairs stored in pool tiles.
@@ -223,108 +230,175 @@ __device__ __forceinline__ void chunk_cumsum(const TIn* __restrict__ g, float* g
 }
 
 // ---------------------------------------------------------------------------
-// Generic K-loop over one or two operand pairs (all M = N = K = 128).
-// Operands come from "row sources": src(row, c0, out16) returns 16 consecutive values of row
-// `row` of the source matrix starting at column c0.
-//   kmaj  : K-major; the source row is the operand's M/N row; every thread stages its own row
-//           (its half of the slice's columns).  Works for TMEM-backed sources.
-//   mn_any: MN-major; the source row is the operand's K row; any thread may fetch any row
-//           (global- or shared-memory-backed sources): (row, 16-column group) items over all
-//           threads.
-//   mn_own: MN-major, TMEM-backed: the two warps owning the slice's lanes stage it, one half of
-//           the MN columns each.
+// Operand staging engine.  A product D (+)= A B (M = N = K = 128) runs in K-slices of 128 bytes
+// per operand row (64 bf16 or 32 tf32 elements).  Every slice of every operand is written by the
+// CTA's threads into 128-byte-swizzled tiles of the operand pool:
+//   K-major tile (A, or B stored [n][k]): 128 rows of 128 bytes, 16-byte chunk j of row r at
+//       chunk position j ^ (r & 7)                       (SWIZZLE_128B, SBO = 1024)
+//   MN-major bf16 tile: atoms of 8 k-rows x 64 MN elements (128 bytes), chunk j of k-row r at
+//       j ^ (r & 7); atoms along MN 1024 bytes apart, along K (8 rows) 2048  (SWIZZLE_128B)
+//   MN-major tf32 tile: SWIZZLE_128B_BASE32B (the only MN-major tf32 layout; see Tile).
+// Each 16-byte chunk position depends on the row, so a warp writing any 8 rows of one chunk
+// column, or one row's 8 chunks, hits all 32 banks: conflict-free for both access patterns below.
+//
+// Operand kinds (all sources return consecutive values of one row of the source matrix):
+//   kmaj  : K-major, TMEM- or shared-memory-backed; the source row is the operand's M/N row and
+//           thread (row, half) stages its own row (src gives 16 values).
+//   kany  : K-major, global-memory-backed; items of 4 consecutive K values laid out so that a
+//           warp's 32 lanes read 512 contiguous bytes (two 256-byte row segments for bf16
+//           slices, four 128-byte ones for tf32) -- fully coalesced (src gives 4 values).
+//   mn_any: MN-major, global-backed; the source row is the operand's K row; a warp reads one
+//           whole 128-element row per item (src gives 4 values).
+//   mn_own: MN-major, TMEM-backed: the two warps owning the slice's K rows (TMEM lanes) stage
+//           it, one half of the MN columns each (src gives 16 values).
 // ---------------------------------------------------------------------------
+enum OpKind { kKOwn = 0, kKAny = 1, kMnAny = 2, kMnOwn = 3 };
 template <class Src>
 struct Opnd {
-  bool mn, any;
+  int kind;
   Src src;
+  __device__ __forceinline__ bool mn() const { return kind >= kMnAny; }
 };
 template <class Src>
-__device__ __forceinline__ Opnd<Src> kmaj(Src s) { return Opnd<Src>{false, false, s}; }
+__device__ __forceinline__ Opnd<Src> kmaj(Src s) { return Opnd<Src>{kKOwn, s}; }
 template <class Src>
-__device__ __forceinline__ Opnd<Src> mn_any(Src s) { return Opnd<Src>{true, true, s}; }
+__device__ __forceinline__ Opnd<Src> kany(Src s) { return Opnd<Src>{kKAny, s}; }
 template <class Src>
-__device__ __forceinline__ Opnd<Src> mn_own(Src s) { return Opnd<Src>{true, false, s}; }
+__device__ __forceinline__ Opnd<Src> mn_any(Src s) { return Opnd<Src>{kMnAny, s}; }
+template <class Src>
+__device__ __forceinline__ Opnd<Src> mn_own(Src s) { return Opnd<Src>{kMnOwn, s}; }
 
-// Work items of one operand slice (KS elements of K) for this thread: kmaj and mn_any operands
-// both give every thread KS / 32 items of 16 values.
-//   kmaj  : item p = columns [k0 + half * KS/2 + 16 p, +16) of the thread's own row
-//   mn_any: item p = (row r, 16-column group) with it = tid + 256 p, r = it % KS, c0 = (it / KS) * 16
-template <class Src>
-__device__ __forceinline__ void fetch_item(const Opnd<Src>& op, int k0, int KS, int p, float* x) {
-  if (!op.mn) {
-    op.src(crow(), k0 + chalf() * (KS >> 1) + p * 16, x);
-  } else if (op.any) {
-    const int it = threadIdx.x + p * kCT;
-    op.src(k0 + it % KS, (it / KS) * 16, x);
+template <int FMT>
+struct SliceShape {
+  static constexpr int KS = FMT == kTF32 ? 32 : 64;  // K elements per slice
+  static constexpr int EB = FMT == kTF32 ? 4 : 2;    // element bytes
+  static constexpr int NOWN = KS / 32;               // 16-value items per thread (kmaj)
+  static constexpr int NANY = KS / 8;                // 4-value items per thread (kany, mn_any)
+};
+
+// Byte offset of element (mn, k) inside a K-major swizzled tile (k < KS).
+template <int FMT>
+__device__ __forceinline__ uint32_t off_k(uint32_t mn, uint32_t k) {
+  const uint32_t kb = k * SliceShape<FMT>::EB;
+  return mn * 128u + ((((kb >> 4) ^ mn) & 7u) << 4) + (kb & 15u);
+}
+// Byte offset of element (mn, k) inside an MN-major tile (MN = 128, k < KS).
+template <int FMT>
+__device__ __forceinline__ uint32_t off_mn(uint32_t mn, uint32_t k) {
+  if constexpr (FMT == kTF32) {
+    return (mn >> 5) * 512u + (k >> 2) * 2048u + (k & 3u) * 128u + (((((mn >> 3) ^ k) & 3u)) << 5) +
+           (mn & 7u) * 4u;
+  } else {
+    return (k >> 3) * 2048u + (mn >> 6) * 1024u + (k & 7u) * 128u + (((((mn >> 3) ^ k) & 7u)) << 4) +
+           (mn & 7u) * 2u;
   }
 }
+
+// Write 4 consecutive values (along the tile's contiguous axis) as hi (and lo) parts.
+template <int FMT>
+__device__ __forceinline__ void put4(uint32_t hi_addr, uint32_t lo_addr, bool lo, const float* v) {
+  if constexpr (FMT == kTF32) {
+    put_piece_t<kTF32>(hi_addr, lo ? lo_addr : 0u, v);
+  } else {
+    uint32_t h[2], l[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      __nv_bfloat162 hv = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+      float2 hf = __bfloat1622float2(hv);
+      __nv_bfloat162 lv = __floats2bfloat162_rn(v[2 * i] - hf.x, v[2 * i + 1] - hf.y);
+      h[i] = *reinterpret_cast<uint32_t*>(&hv);
+      l[i] = *reinterpret_cast<uint32_t*>(&lv);
+    }
+    asm volatile("st.shared.v2.b32 [%0], {%1,%2};" ::"r"(hi_addr), "r"(h[0]), "r"(h[1]) : "memory");
+    if (lo) asm volatile("st.shared.v2.b32 [%0], {%1,%2};" ::"r"(lo_addr), "r"(l[0]), "r"(l[1]) : "memory");
+  }
+}
+// Write 16 consecutive values (4 calls of put4 worth) along the contiguous axis.
+template <int FMT>
+__device__ __forceinline__ void put16_k(const Tile tt[2], bool lo, uint32_t mn, uint32_t k0, const float* v) {
+  constexpr int W = FMT == kTF32 ? 4 : 8;
+#pragma unroll
+  for (int i = 0; i < 16; i += W) {
+    const uint32_t o = off_k<FMT>(mn, k0 + i);
+    put_piece_t<FMT>(tt[0].addr + o, lo ? tt[1].addr + o : 0u, v + i);
+  }
+}
+template <int FMT>
+__device__ __forceinline__ void put16_mn(const Tile tt[2], bool lo, uint32_t mn0, uint32_t k, const float* v) {
+  constexpr int W = FMT == kTF32 ? 4 : 8;
+#pragma unroll
+  for (int i = 0; i < 16; i += W) {
+    const uint32_t o = off_mn<FMT>(mn0 + i, k);
+    put_piece_t<FMT>(tt[0].addr + o, lo ? tt[1].addr + o : 0u, v + i);
+  }
+}
+
+// Coalesced item p of this thread: float index e of the slice's source block in row-major order.
+__device__ __forceinline__ int any_e(int p) { return (p * kCT + (int)threadIdx.x) * 4; }
+
+// Loads of one operand slice into registers (x holds 32 values: 2 x 16 or 8 x 4).
 template <int FMT, class Src>
-__device__ __forceinline__ void store_item(const Tile tt[2], const Opnd<Src>& op, bool lo, int KS, int p,
-                                           const float* x) {
-  if (!op.mn) {
-    stage_krow_t<FMT, 16>(tt[0], tt[1], lo, (uint32_t)crow(), chalf() * (KS >> 1) + p * 16, x);
-  } else if (op.any) {
-    const int it = threadIdx.x + p * kCT;
-    stage_mnrow_t<FMT, 16>(tt[0], tt[1], lo, (uint32_t)(it % KS), (it / KS) * 16, x);
+__device__ __forceinline__ void fetch_op(const Opnd<Src>& op, int k0, float* x) {
+  using S = SliceShape<FMT>;
+  if (op.kind == kKOwn) {
+#pragma unroll
+    for (int p = 0; p < S::NOWN; ++p) op.src(crow(), k0 + chalf() * (S::KS / 2) + 16 * p, x + 16 * p);
+  } else if (op.kind == kKAny) {
+#pragma unroll
+    for (int p = 0; p < S::NANY; ++p) {
+      const int e = any_e(p);
+      op.src(e / S::KS, k0 + e % S::KS, x + 4 * p);
+    }
+  } else if (op.kind == kMnAny) {
+#pragma unroll
+    for (int p = 0; p < S::NANY; ++p) {
+      const int e = any_e(p);
+      op.src(k0 + (e >> 7), e & 127, x + 4 * p);
+    }
+  }
+}
+// Shared-memory stores of one operand slice from registers.
+template <int FMT, class Src>
+__device__ __forceinline__ void store_op(const Tile tt[2], const Opnd<Src>& op, bool lo, const float* x) {
+  using S = SliceShape<FMT>;
+  if (op.kind == kKOwn) {
+#pragma unroll
+    for (int p = 0; p < S::NOWN; ++p) put16_k<FMT>(tt, lo, (uint32_t)crow(), chalf() * (S::KS / 2) + 16 * p, x + 16 * p);
+  } else if (op.kind == kKAny) {
+#pragma unroll
+    for (int p = 0; p < S::NANY; ++p) {
+      const int e = any_e(p);
+      const uint32_t o = off_k<FMT>((uint32_t)(e / S::KS), (uint32_t)(e % S::KS));
+      put4<FMT>(tt[0].addr + o, tt[1].addr + o, lo, x + 4 * p);
+    }
+  } else if (op.kind == kMnAny) {
+#pragma unroll
+    for (int p = 0; p < S::NANY; ++p) {
+      const int e = any_e(p);
+      const uint32_t o = off_mn<FMT>((uint32_t)(e & 127), (uint32_t)(e >> 7));
+      put4<FMT>(tt[0].addr + o, tt[1].addr + o, lo, x + 4 * p);
+    }
   }
 }
 // TMEM-backed MN-major operands: the two warps owning the slice's lanes, one half of MN each.
 template <int FMT, class Src>
-__device__ __forceinline__ void stage_own(const Tile tt[2], const Opnd<Src>& op, bool lo, int k0, int KS) {
+__device__ __forceinline__ void stage_own(const Tile tt[2], const Opnd<Src>& op, bool lo, int k0) {
   const int warp = threadIdx.x >> 5;
-  if (op.mn && !op.any && (warp & 3) * 32 >= k0 && (warp & 3) * 32 < k0 + KS) {
+  if (op.kind == kMnOwn && (warp & 3) * 32 >= k0 && (warp & 3) * 32 < k0 + SliceShape<FMT>::KS) {
     const int row = crow(), half = chalf();
 #pragma unroll 1
     for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 16) {
       float x[16];
       op.src(row, c0, x);
-      stage_mnrow_t<FMT, 16>(tt[0], tt[1], lo, (uint32_t)(row - k0), c0, x);
+      put16_mn<FMT>(tt, lo, (uint32_t)c0, (uint32_t)(row - k0), x);
     }
   }
 }
 
-// Register buffer for the prefetched items of one slice: up to two items (KS / 32) of two operands.
+// Register buffer for the prefetched slice of operands 1-2.
 struct Prefetch {
-  float x[2][2][16];
+  float x[2][32];
 };
-template <class S1, class S2>
-__device__ __forceinline__ void prefetch2(Prefetch& pf, const Opnd<S1>& o1, const Opnd<S2>& o2, int k0, int KS) {
-  const int np = KS / 32;
-#pragma unroll
-  for (int p = 0; p < 2; ++p) {
-    if (p < np) {
-      fetch_item(o1, k0, KS, p, pf.x[0][p]);
-      fetch_item(o2, k0, KS, p, pf.x[1][p]);
-    }
-  }
-}
-template <int FMT, class S1, class S2>
-__device__ __forceinline__ void store2_t(const Prefetch& pf, const Tile* t1, const Opnd<S1>& o1, const Tile* t2,
-                                         const Opnd<S2>& o2, bool lo, int KS) {
-  const int np = KS / 32;
-#pragma unroll
-  for (int p = 0; p < 2; ++p) {
-    if (p < np) {
-      store_item<FMT>(t1, o1, lo, KS, p, pf.x[0][p]);
-      store_item<FMT>(t2, o2, lo, KS, p, pf.x[1][p]);
-    }
-  }
-}
-// Stage operands 3 and 4 (not prefetched) of one slice: loads of both issued before the stores.
-template <int FMT, class S3, class S4>
-__device__ __forceinline__ void stage34_t(const Tile* t3, const Opnd<S3>& o3, const Tile* t4, const Opnd<S4>& o4,
-                                          int nops, bool lo, int k0, int KS) {
-  const int np = KS / 32;
-#pragma unroll 1
-  for (int p = 0; p < np; ++p) {
-    float x3[16], x4[16];
-    if (nops > 2) fetch_item(o3, k0, KS, p, x3);
-    if (nops > 3) fetch_item(o4, k0, KS, p, x4);
-    if (nops > 2) store_item<FMT>(t3, o3, lo, KS, p, x3);
-    if (nops > 3) store_item<FMT>(t4, o4, lo, KS, p, x4);
-  }
-}
 
 // One K-loop of up to four operands (ops 1-2: pair 1's A and B, or A1 and the shared B; ops 3-4:
 // the rest).  Software-pipelined: the global / shared loads of ops 1-2 for slice s+1 are issued
@@ -333,18 +407,27 @@ __device__ __forceinline__ void stage34_t(const Tile* t3, const Opnd<S3>& o3, co
 template <int FMT, class S1, class S2, class S3, class S4, class Issue>
 __device__ __forceinline__ void kloop_t(MmaBar& mb, const Tile* t1, const Opnd<S1>& o1, const Tile* t2,
                                         const Opnd<S2>& o2, const Tile* t3, const Opnd<S3>& o3, const Tile* t4,
-                                        const Opnd<S4>& o4, int nops, bool lo, int KS, Issue issue) {
-  const int ns = 128 / KS;
+                                        const Opnd<S4>& o4, int nops, bool lo, Issue issue) {
+  constexpr int KS = SliceShape<FMT>::KS;
+  constexpr int ns = 128 / KS;
   Prefetch pf;
-  prefetch2(pf, o1, o2, 0, KS);
+  fetch_op<FMT>(o1, 0, pf.x[0]);
+  fetch_op<FMT>(o2, 0, pf.x[1]);
   for (int s = 0; s < ns; ++s) {
     const int k0 = s * KS;
-    store2_t<FMT>(pf, t1, o1, t2, o2, lo, KS);
-    stage34_t<FMT>(t3, o3, t4, o4, nops, lo, k0, KS);
-    stage_own<FMT>(t1, o1, lo, k0, KS);
-    stage_own<FMT>(t2, o2, lo, k0, KS);
-    if (nops > 2) stage_own<FMT>(t3, o3, lo, k0, KS);
-    if (nops > 3) stage_own<FMT>(t4, o4, lo, k0, KS);
+    store_op<FMT>(t1, o1, lo, pf.x[0]);
+    store_op<FMT>(t2, o2, lo, pf.x[1]);
+    if (nops > 2) {
+      float x3[32], x4[32];
+      fetch_op<FMT>(o3, k0, x3);
+      if (nops > 3) fetch_op<FMT>(o4, k0, x4);
+      store_op<FMT>(t3, o3, lo, x3);
+      if (nops > 3) store_op<FMT>(t4, o4, lo, x4);
+    }
+    stage_own<FMT>(t1, o1, lo, k0);
+    stage_own<FMT>(t2, o2, lo, k0);
+    if (nops > 2) stage_own<FMT>(t3, o3, lo, k0);
+    if (nops > 3) stage_own<FMT>(t4, o4, lo, k0);
     staged_sync();
     if (threadIdx.x == 0) {
       tc_fence_after();
@@ -352,7 +435,10 @@ __device__ __forceinline__ void kloop_t(MmaBar& mb, const Tile* t1, const Opnd<S
       mma_commit(mb.bar);
     }
     __syncwarp();
-    if (s + 1 < ns) prefetch2(pf, o1, o2, k0 + KS, KS);
+    if (s + 1 < ns) {
+      fetch_op<FMT>(o1, k0 + KS, pf.x[0]);
+      fetch_op<FMT>(o2, k0 + KS, pf.x[1]);
+    }
     mbar_wait(mb.bar, mb.phase, mb.status);
     mb.phase ^= 1u;
     tc_fence_after();
@@ -367,16 +453,15 @@ struct NoSrc {
 template <class SA, class SB>
 __device__ __forceinline__ void gemm1(Mode m, uint32_t pool, MmaBar& mb, uint32_t d, const Opnd<SA>& a,
                                       const Opnd<SB>& b, bool neg, bool acc) {
-  const int KS = kslice(m);
   Tile A[2], B[2];
-  A[0] = a.mn ? pool_mn(pool, 0, m) : pool_k(pool, 0);
-  A[1] = a.mn ? pool_mn(pool, 1, m) : pool_k(pool, 1);
-  B[0] = b.mn ? pool_mn(pool, 2, m) : pool_k(pool, 2);
-  B[1] = b.mn ? pool_mn(pool, 3, m) : pool_k(pool, 3);
+  A[0] = a.mn() ? pool_mn(pool, 0, m) : pool_k(pool, 0);
+  A[1] = a.mn() ? pool_mn(pool, 1, m) : pool_k(pool, 1);
+  B[0] = b.mn() ? pool_mn(pool, 2, m) : pool_k(pool, 2);
+  B[1] = b.mn() ? pool_mn(pool, 3, m) : pool_k(pool, 3);
   auto issue = [&](int s) { issue_slice(m, d, A, B, 128, neg, acc || s > 0); };
   const bool lo = m.passes == 3;
-  if (m.fmt == kTF32) kloop_t<kTF32>(mb, A, a, B, b, A, a, B, b, 2, lo, KS, issue);
-  else kloop_t<kBF16>(mb, A, a, B, b, A, a, B, b, 2, lo, KS, issue);
+  if (m.fmt == kTF32) kloop_t<kTF32>(mb, A, a, B, b, A, a, B, b, 2, lo, issue);
+  else kloop_t<kBF16>(mb, A, a, B, b, A, a, B, b, 2, lo, issue);
 }
 
 // Two products sharing the K-slicing: D1 (+)= A1 B1 and D2 (+)= A2 B2, where pair 2 reuses pair 1's
@@ -386,31 +471,38 @@ __device__ __forceinline__ void gemm2(Mode m, uint32_t pool, MmaBar& mb, uint32_
                                       const Opnd<SB1>& b1, bool neg1, bool acc1, uint32_t d2,
                                       const Opnd<SA2>& a2, const Opnd<SB2>& b2, bool neg2, bool acc2,
                                       bool share_a, bool share_b) {
-  const int KS = kslice(m);
   auto tiles = [&](int i, bool mn, Tile out[2]) {
     out[0] = mn ? pool_mn(pool, i, m) : pool_k(pool, i);
     out[1] = mn ? pool_mn(pool, i + 1, m) : pool_k(pool, i + 1);
   };
   Tile A1[2], B1[2], A2[2], B2[2];
-  tiles(0, a1.mn, A1);
-  tiles(2, b1.mn, B1);
+  tiles(0, a1.mn(), A1);
+  tiles(2, b1.mn(), B1);
   int nt = 4;
-  if (share_a) { A2[0] = A1[0]; A2[1] = A1[1]; } else { tiles(nt, a2.mn, A2); nt += 2; }
-  if (share_b) { B2[0] = B1[0]; B2[1] = B1[1]; } else { tiles(nt, b2.mn, B2); nt += 2; }
+  if (share_a) { A2[0] = A1[0]; A2[1] = A1[1]; } else { tiles(nt, a2.mn(), A2); nt += 2; }
+  if (share_b) { B2[0] = B1[0]; B2[1] = B1[1]; } else { tiles(nt, b2.mn(), B2); nt += 2; }
   auto issue = [&](int s) {
     issue_slice(m, d1, A1, B1, 128, neg1, acc1 || s > 0);
     issue_slice(m, d2, A2, B2, 128, neg2, acc2 || s > 0);
   };
   const bool lo = m.passes == 3;
   if (m.fmt == kTF32) {
-    if (share_a) kloop_t<kTF32>(mb, A1, a1, B1, b1, B2, b2, B2, b2, 3, lo, KS, issue);
-    else if (share_b) kloop_t<kTF32>(mb, A1, a1, B1, b1, A2, a2, A2, a2, 3, lo, KS, issue);
-    else kloop_t<kTF32>(mb, A1, a1, B1, b1, A2, a2, B2, b2, 4, lo, KS, issue);
+    if (share_a) kloop_t<kTF32>(mb, A1, a1, B1, b1, B2, b2, B2, b2, 3, lo, issue);
+    else if (share_b) kloop_t<kTF32>(mb, A1, a1, B1, b1, A2, a2, A2, a2, 3, lo, issue);
+    else kloop_t<kTF32>(mb, A1, a1, B1, b1, A2, a2, B2, b2, 4, lo, issue);
   } else {
-    if (share_a) kloop_t<kBF16>(mb, A1, a1, B1, b1, B2, b2, B2, b2, 3, lo, KS, issue);
-    else if (share_b) kloop_t<kBF16>(mb, A1, a1, B1, b1, A2, a2, A2, a2, 3, lo, KS, issue);
-    else kloop_t<kBF16>(mb, A1, a1, B1, b1, A2, a2, B2, b2, 4, lo, KS, issue);
+    if (share_a) kloop_t<kBF16>(mb, A1, a1, B1, b1, B2, b2, B2, b2, 3, lo, issue);
+    else if (share_b) kloop_t<kBF16>(mb, A1, a1, B1, b1, A2, a2, A2, a2, 3, lo, issue);
+    else kloop_t<kBF16>(mb, A1, a1, B1, b1, A2, a2, B2, b2, 4, lo, issue);
   }
+}
+
+// 4-value row loaders of the coalesced (kany / mn_any) sources
+template <class TIn>
+__device__ __forceinline__ void ld4_in(const TIn* p, float* x) { ld4(p, x); }
+__device__ __forceinline__ void ld4_f(const float* p, float* x) {
+  const float4 v = *reinterpret_cast<const float4*>(p);
+  x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
 }
 
 // ---------------------------------------------------------------------------

@@ -154,3 +154,98 @@ extern "C" gdn2_status gdn2_selftest_gemm(const float* A, const float* B, float*
       A, B, C, N, precision, a_mode, b_mn, dev_status);
   return cudaGetLastError() == cudaSuccess ? GDN2_OK : GDN2_ERR_CUDA;
 }
+
+// ---------------------------------------------------------------------------------------------
+// Self-test of the chunk kernels' staging engine (swizzled pool tiles, operand kinds): one
+// 128 x 128 x 128 product C = A B through gemm1, A and B taken from global memory as K-major
+// own-row (kmaj), K-major coalesced (kany) or MN-major coalesced (mn_any) operands.
+// ---------------------------------------------------------------------------------------------
+#include "gdn2_kernels.cuh"
+
+namespace gdn2 {
+
+constexpr uint32_t kEngineSmem = 1024 + 4 * 16384 + 64;
+
+template <int AK, int BK>
+__global__ void __launch_bounds__(kCT, 1)
+    selftest_engine_kernel(const float* __restrict__ A, const float* __restrict__ At, const float* __restrict__ B,
+                           const float* __restrict__ Bt, float* __restrict__ C, int prec, unsigned* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t pool = smem_u32(sm);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + 4 * 16384);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 1);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  if (warp == 0) {
+    tmem_alloc(tslot, 128);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tb = *tslot;
+  MmaBar mb{bar, 0u, status};
+  const Mode m = mode_from_enum(prec);
+  // operand rows: A row m = A[m][:], A^T row k = At[k][:], B^T row n = Bt[n][:], B row k = B[k][:]
+  auto a16 = [&](int r, int c0, float* x) { ld16_f(A + r * 128 + c0, x); };
+  auto a4 = [&](int r, int c0, float* x) { ld4_f(A + r * 128 + c0, x); };
+  auto at4 = [&](int r, int c0, float* x) { ld4_f(At + r * 128 + c0, x); };
+  auto b16 = [&](int r, int c0, float* x) { ld16_f(Bt + r * 128 + c0, x); };
+  auto b4 = [&](int r, int c0, float* x) { ld4_f(Bt + r * 128 + c0, x); };
+  auto bk4 = [&](int r, int c0, float* x) { ld4_f(B + r * 128 + c0, x); };
+  auto run = [&](auto aop) {
+    if constexpr (BK == 0) gemm1(m, pool, mb, tb, aop, kmaj(b16), false, false);
+    else if constexpr (BK == 1) gemm1(m, pool, mb, tb, aop, kany(b4), false, false);
+    else gemm1(m, pool, mb, tb, aop, mn_any(bk4), false, false);
+  };
+  if constexpr (AK == 0) run(kmaj(a16));
+  else if constexpr (AK == 1) run(kany(a4));
+  else run(mn_any(at4));
+  const int t = crow(), cb = chalf() * 64;
+  for (int c0 = cb; c0 < cb + 64; c0 += 16) {
+    float x[16];
+    tmem_ld16(tb, (uint32_t)c0, x);
+    st16_f(C + t * 128 + c0, x);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tb, 128);
+}
+
+template <int AK, int BK>
+static cudaError_t launch_engine(const float* A, const float* At, const float* B, const float* Bt, float* C, int prec,
+                                 unsigned* st, cudaStream_t s) {
+  cudaError_t e = cudaFuncSetAttribute(selftest_engine_kernel<AK, BK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)kEngineSmem);
+  if (e != cudaSuccess) return e;
+  selftest_engine_kernel<AK, BK><<<1, kCT, kEngineSmem, s>>>(A, At, B, Bt, C, prec, st);
+  return cudaGetLastError();
+}
+template <int AK>
+static cudaError_t launch_engine_b(int bk, const float* A, const float* At, const float* B, const float* Bt, float* C,
+                                   int prec, unsigned* st, cudaStream_t s) {
+  if (bk == 0) return launch_engine<AK, 0>(A, At, B, Bt, C, prec, st, s);
+  if (bk == 1) return launch_engine<AK, 1>(A, At, B, Bt, C, prec, st, s);
+  return launch_engine<AK, 2>(A, At, B, Bt, C, prec, st, s);
+}
+
+}  // namespace gdn2
+
+extern "C" gdn2_status gdn2_selftest_engine(const float* A, const float* At, const float* B, const float* Bt, float* C,
+                                            int32_t precision, int32_t a_kind, int32_t b_kind, uint32_t* dev_status,
+                                            void* stream) {
+  using namespace gdn2;
+  if (!A || !At || !B || !Bt || !C || !dev_status) return GDN2_ERR_INVALID_ARGUMENT;
+  if (precision < 0 || precision > 3 || a_kind < 0 || a_kind > 2 || b_kind < 0 || b_kind > 2)
+    return GDN2_ERR_INVALID_ARGUMENT;
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaError_t e;
+  if (a_kind == 0) e = launch_engine_b<0>(b_kind, A, At, B, Bt, C, precision, dev_status, s);
+  else if (a_kind == 1) e = launch_engine_b<1>(b_kind, A, At, B, Bt, C, precision, dev_status, s);
+  else e = launch_engine_b<2>(b_kind, A, At, B, Bt, C, precision, dev_status, s);
+  return e == cudaSuccess ? GDN2_OK : GDN2_ERR_CUDA;
+}

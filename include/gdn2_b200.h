@@ -124,6 +124,16 @@ const char* gdn2_status_string(gdn2_status status);
 gdn2_status gdn2_selftest_gemm(const float* A, const float* B, float* C, int32_t N, int32_t precision,
                                int32_t a_mode, int32_t b_mn, uint32_t* dev_status, void* stream);
 
+/*
+ * Self-test of the chunk kernels' operand staging engine (no reference counterpart): C = A B for
+ * 128 x 128 fp32 matrices through one tensor-core product of the given precision, with A staged
+ * as a K-major own-row (a_kind 0), K-major coalesced (1) or MN-major coalesced (2) operand and B
+ * likewise (b_kind).  At and Bt are the transposes of A and B (row-major, device memory).
+ */
+gdn2_status gdn2_selftest_engine(const float* A, const float* At, const float* B, const float* Bt, float* C,
+                                 int32_t precision, int32_t a_kind, int32_t b_kind, uint32_t* dev_status,
+                                 void* stream);
+
 /* Allocation-free forward (no counterpart in the reference).  Same arguments and results as
  * gdn2_fwd minus the residual buffer: the scratch lives in a fixed 64 MiB device array inside the
  * library, so the call performs no device allocation.  It is meant for callers that cannot
