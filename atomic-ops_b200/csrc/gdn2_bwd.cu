@@ -104,18 +104,20 @@ __global__ void __launch_bounds__(kCT, 1) bwd_pre_kernel(const BwdParams P) {
   // S0 = Aqk^T do, S1 = (scale qg)^T do   (shared B = do)
   gemm2(m3, pool, mb, S0, mn_any(src_aqk), mn_any(src_do), false, false, S1, mn_any(src_qg), mn_any(NoSrc()), false,
         false, false, true);
-  for (int c0 = cb; c0 < cb + 64; c0 += 16) {
-    float x[16];
-    tmem_ld16(S0, c0, x);
-    st16_f(dvl_g + t * kD + c0, x);
+  {
+    float* xb = xbuf(sm);
+    tmem_to_xbuf(S0, cb, xb);
+    xb_flush(xb, dvl_g, kD, cb);
   }
+  __syncthreads();  // the buffers live in the operand pool the next product stages into
   // S1 -= wp^T dvl
   gemm1(m3, pool, mb, S1, mn_any(src_wp), mn_own(tm0), true, true);
-  for (int c0 = cb; c0 < cb + 64; c0 += 16) {
-    float x[16];
-    tmem_ld16(S1, c0, x);
-    st16_f(cc_g + t * kD + c0, x);
+  {
+    float* xb = xbuf(sm);
+    tmem_to_xbuf(S1, cb, xb);
+    xb_flush(xb, cc_g, kD, cb);
   }
+  __syncthreads();
   // transposed transition of this chunk for the reverse scan: M^T = diag(e^gl) - wp^T kg
   gemm1(m3, pool, mb, S0, mn_any(src_wp), mn_any(src_kg), false, false);
   {
@@ -380,6 +382,7 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
   // 10.-11. finish dq and db;  S3 <- dgc partial;  S0 <- Dbk b E (pre-scaled dk partial)
   {
     const float* gr = gcrow(t);
+    float* xb = xbuf(sm);
 #pragma unroll 1
     for (int hh = 0; hh < 2; ++hh) {
       float q2[32], k2[32], b2[32];
@@ -405,7 +408,7 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
           y[j] = sanitize(x[j], clip);
           dgcp[j] = qv[j] * x[j];
         }
-        st16_out(dq + t * kD + c0, y);
+        xb2_put16(xb, 0, 16 * jj, y);
         tmem_ld16(S0, c0, x);  // Dbk / E
   #pragma unroll
         for (int j = 0; j < 16; ++j) {
@@ -414,10 +417,12 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
           dgcp[j] += 2.f * bv[j] * kv[j] * x[j];
           x[j] = x[j] * bv[j] * E[j];
         }
-        st16_out(db + t * kD + c0, y);
+        xb2_put16(xb, 1, 16 * jj, y);
         tmem_st16(S3, c0, dgcp);
         tmem_st16(S0, c0, x);
       }
+      xb2_flush(xb, 0, dq, kD, cb + 32 * hh);
+      xb2_flush(xb, 1, db, kD, cb + 32 * hh);
     }
   }
   sync_all();
@@ -446,10 +451,11 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
         dgcp[j] -= kv[j] * x[j];
         if (t == kT - 1) dgcp[j] += extra_s[c0 + j] + extra_s[kD + c0 + j];
       }
-      st16_out(dk + t * kD + c0, y);
+      xb_put16(xbuf(sm), c0 - cb, y);
 #pragma unroll
       for (int j = 0; j < 16; ++j) gr[c0 + j] = dgcp[j];
     }
+    xb_flush(xbuf(sm), dk, kD, cb);
   }
   __syncthreads();
   // 14. dg = reverse cumsum of dgc over the chunk (B5)

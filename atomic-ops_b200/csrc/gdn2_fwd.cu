@@ -178,12 +178,13 @@ __global__ void __launch_bounds__(kCT, 1) fwd_intra_kernel(const OpParams p) {
   {
     const float keep = 1.0f - p.eps;
     const int blk = t >> 5;
+    float* xb = xbuf(sm);
     for (int c0 = cb; c0 < cb + 64; c0 += 16) {
       float x[16];
       tmem_ld16(S0, c0, x);
 #pragma unroll
       for (int j = 0; j < 16; ++j) x[j] = (c0 + j <= t) ? sanitize(p.scale * x[j], clip) : 0.f;
-      st16_f(aqk_g + t * kT + c0, x);
+      xb_put16(xb, c0 - cb, x);
       tmem_ld16(S1, c0, x);
 #pragma unroll
       for (int j = 0; j < 16; ++j) x[j] = (c0 + j < t) ? keep * sanitize(x[j], clip) : 0.f;
@@ -193,6 +194,7 @@ __global__ void __launch_bounds__(kCT, 1) fwd_intra_kernel(const OpParams p) {
         for (int j = 0; j < 16; ++j) dsm[blk * 1056 + (t & 31) * 33 + (c0 & 31) + j] = x[j];
       }
     }
+    xb_flush(xb, aqk_g, kT, cb);
   }
   tc_fence_before();
   __syncthreads();
@@ -231,14 +233,18 @@ __global__ void __launch_bounds__(kCT, 1) fwd_intra_kernel(const OpParams p) {
   __syncthreads();
   tc_fence_after();
   gemm1(ms, pool, mbar, S2, kmaj(tm(S0)), mn_own(tm(S3)), false, false);    // W P -> S2
-  for (int c0 = cb; c0 < cb + 64; c0 += 16) {                               // A = sanitize(P - W P)
-    float x[16], y[16];
-    tmem_ld16(S3, c0, x);
-    tmem_ld16(S2, c0, y);
+  {
+    float* xb = xbuf(sm);
+    for (int c0 = cb; c0 < cb + 64; c0 += 16) {                             // A = sanitize(P - W P)
+      float x[16], y[16];
+      tmem_ld16(S3, c0, x);
+      tmem_ld16(S2, c0, y);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) x[j] = (c0 + j <= t) ? sanitize(x[j] - y[j], clip) : 0.f;
-    tmem_st16(S1, c0, x);
-    st16_f(ainv_g + t * kT + c0, x);
+      for (int j = 0; j < 16; ++j) x[j] = (c0 + j <= t) ? sanitize(x[j] - y[j], clip) : 0.f;
+      tmem_st16(S1, c0, x);
+      xb_put16(xb, c0 - cb, x);
+    }
+    xb_flush(xb, ainv_g, kT, cb);
   }
   tc_fence_before();
   __syncthreads();
@@ -247,18 +253,21 @@ __global__ void __launch_bounds__(kCT, 1) fwd_intra_kernel(const OpParams p) {
   // ---- 8. wp = A (b k e^gc) -> S0,  u = A (w v) -> S2                          (dot mode) --------
   gemm2(md, pool, mbar, S0, kmaj(tm(S1)), mn_any(src_kb), false, false, S2, kmaj(NoSrc()), mn_any(src_wv), false,
         false, true, false);
-  for (int c0 = cb; c0 < cb + 64; c0 += 16) {
-    float x[16];
-    tmem_ld16(S0, c0, x);
+  {
+    float* xb = xbuf(sm);
+#pragma unroll 1
+    for (int pass = 0; pass < 2; ++pass) {
+      const uint32_t slot = pass ? S2 : S0;
+      for (int c0 = cb; c0 < cb + 64; c0 += 16) {
+        float x[16];
+        tmem_ld16(slot, c0, x);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) x[j] = sanitize(x[j], clip);
-    tmem_st16(S0, c0, x);
-    st16_f(wp_g + t * kD + c0, x);
-    tmem_ld16(S2, c0, x);
-#pragma unroll
-    for (int j = 0; j < 16; ++j) x[j] = sanitize(x[j], clip);
-    tmem_st16(S2, c0, x);
-    st16_f(u_g + t * kD + c0, x);
+        for (int j = 0; j < 16; ++j) x[j] = sanitize(x[j], clip);
+        tmem_st16(slot, c0, x);
+        xb_put16(xb, c0 - cb, x);
+      }
+      xb_flush(xb, pass ? u_g : wp_g, kD, cb);
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -277,8 +286,9 @@ __global__ void __launch_bounds__(kCT, 1) fwd_intra_kernel(const OpParams p) {
       image_store8(mf_g, md, t, c0, x);
       image_store8(mf_g, md, t, c0 + 8, x + 8);
       tmem_ld16(S3, c0, x);
-      st16_f(bc_g + t * kD + c0, x);
+      xb_put16(xbuf(sm), c0 - cb, x);
     }
+    xb_flush(xbuf(sm), bc_g, kD, cb);
   }
 
   tc_fence_before();
@@ -350,26 +360,38 @@ __global__ void __launch_bounds__(kCT, 1) fwd_out_kernel(const OpParams p, float
   gemm2(md, pool, mbar, S0, kany(src_wp), mn_any(src_h), false, false, S1, kany(src_qg), mn_any(NoSrc()), false,
         false, false, true);
   // v_new = u - S0 (kept in S0 and written as a residual)
-  for (int c0 = cb; c0 < cb + 64; c0 += 16) {
-    float x[16], uv[16];
-    tmem_ld16(S0, c0, x);
-    ld16_f(u_g + t * kD + c0, uv);
+  {
+    float uv[64];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) x[j] = uv[j] - x[j];
-    st16_f(vn_g + t * kD + c0, x);
-    tmem_st16(S0, c0, x);
+    for (int j = 0; j < 4; ++j) ld16_f(u_g + t * kD + cb + 16 * j, uv + 16 * j);
+    float* xb = xbuf(sm);
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+      const int c0 = cb + 16 * jj;
+      float x[16];
+      tmem_ld16(S0, c0, x);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) x[j] = uv[16 * jj + j] - x[j];
+      xb_put16(xb, c0 - cb, x);
+      tmem_st16(S0, c0, x);
+    }
+    xb_flush(xb, vn_g, kD, cb);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   // S1 += Aqk v_new
   gemm1(md, pool, mbar, S1, kany(src_aqk), mn_own(tm0), false, true);
-  for (int c0 = cb; c0 < cb + 64; c0 += 16) {
-    float x[16];
-    tmem_ld16(S1, c0, x);
+  {
+    float* xb = xbuf(sm);
+    for (int c0 = cb; c0 < cb + 64; c0 += 16) {
+      float x[16];
+      tmem_ld16(S1, c0, x);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) x[j] = sanitize(x[j], clip);
-    st16_f(o_g + t * kD + c0, x);
+      for (int j = 0; j < 16; ++j) x[j] = sanitize(x[j], clip);
+      xb_put16(xb, c0 - cb, x);
+    }
+    xb_flush(xb, o_g, kD, cb);
   }
   tc_fence_before();
   __syncthreads();

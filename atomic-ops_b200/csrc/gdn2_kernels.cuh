@@ -512,9 +512,11 @@ __device__ __forceinline__ void ld4_f(const float* p, float* x) {
 // which lane l handles 4 consecutive columns of two rows per step (rows 2i + l / 16): each
 // warp-wide access then covers two contiguous 256-byte row segments.
 // ---------------------------------------------------------------------------
-constexpr int kXPitch = 68;  // floats per buffered row (64 + 4: conflict-free 16-byte accesses)
+constexpr int kXPitch = 68;   // floats per buffered row of a 32 x 64 block (conflict-free 16-byte accesses)
+constexpr int kXPitch2 = 36;  // floats per buffered row of a 32 x 32 block
+constexpr int kXSlot = 2304;  // floats per warp: one 32 x 64 block or two 32 x 32 blocks
 __device__ __forceinline__ float* xbuf(uint8_t* pool_base) {
-  return reinterpret_cast<float*>(pool_base) + (threadIdx.x >> 5) * 32 * kXPitch;
+  return reinterpret_cast<float*>(pool_base) + (threadIdx.x >> 5) * kXSlot;
 }
 // This thread's 64-column half-row [cb, cb + 64) of TMEM slot `slot` -> the warp's buffer, row = lane.
 __device__ __forceinline__ void tmem_to_xbuf(uint32_t slot, int cb, float* xb) {
@@ -532,6 +534,49 @@ __device__ __forceinline__ void tmem_to_xbuf(uint32_t slot, int cb, float* xb) {
 // Coalesced position of step i (0..15): the warp-local row (0..31) and column offset (0..60).
 __device__ __forceinline__ int xrow(int i) { return 2 * i + ((threadIdx.x & 31) >> 4); }
 __device__ __forceinline__ int xcol() { return 4 * (threadIdx.x & 15); }
+// Row-layout results into the buffer: this thread's row (its lane), 16 columns at local column c.
+__device__ __forceinline__ void xb_put16(float* xb, int c, const float* x) {
+  float* row = xb + (threadIdx.x & 31) * kXPitch + c;
+#pragma unroll
+  for (int i = 0; i < 16; i += 4) *reinterpret_cast<float4*>(row + i) = make_float4(x[i], x[i + 1], x[i + 2], x[i + 3]);
+}
+// 32-column variant: this thread's row, 16 columns at local column c (0 or 16) of block `blk` (0/1).
+__device__ __forceinline__ void xb2_put16(float* xb, int blk, int c, const float* x) {
+  float* row = xb + blk * 32 * kXPitch2 + (threadIdx.x & 31) * kXPitch2 + c;
+#pragma unroll
+  for (int i = 0; i < 16; i += 4) *reinterpret_cast<float4*>(row + i) = make_float4(x[i], x[i + 1], x[i + 2], x[i + 3]);
+}
+// Buffered 32 x 32 block `blk` -> global rows 32 (warp & 3) + r, columns c0..c0+31 (four 128-byte
+// row segments per warp-wide store).
+template <class TOut>
+__device__ __forceinline__ void xb2_flush(float* xb, int blk, TOut* dst, int ld, int c0) {
+  __syncwarp();
+  const int r0 = ((threadIdx.x >> 5) & 3) * 32, lane = threadIdx.x & 31;
+  const float* b = xb + blk * 32 * kXPitch2;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int lr = 4 * i + (lane >> 3), lc = 4 * (lane & 7);
+    const float4 v4 = *reinterpret_cast<const float4*>(b + lr * kXPitch2 + lc);
+    const float v[4] = {v4.x, v4.y, v4.z, v4.w};
+    st4(dst + (size_t)(r0 + lr) * ld + c0 + lc, v);
+  }
+  __syncwarp();
+}
+// The warp's buffered 32 x 64 block -> global rows 32 (warp & 3) + r, columns cb..cb+63 of a
+// matrix with row stride ld (coalesced: each warp-wide store covers two 256-byte row segments).
+template <class TOut>
+__device__ __forceinline__ void xb_flush(float* xb, TOut* dst, int ld, int cb) {
+  __syncwarp();
+  const int r0 = ((threadIdx.x >> 5) & 3) * 32;
+#pragma unroll 8
+  for (int i = 0; i < 16; ++i) {
+    const int lr = xrow(i);
+    const float4 v4 = *reinterpret_cast<const float4*>(xb + lr * kXPitch + xcol());
+    const float v[4] = {v4.x, v4.y, v4.z, v4.w};
+    st4(dst + (size_t)(r0 + lr) * ld + cb + xcol(), v);
+  }
+  __syncwarp();
+}
 
 // Row loaders (16 values)
 template <class TIn>
