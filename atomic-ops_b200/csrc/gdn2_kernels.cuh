@@ -410,14 +410,24 @@ __device__ __forceinline__ void kloop_t(MmaBar& mb, const Tile* t1, const Opnd<S
                                         const Opnd<S4>& o4, int nops, bool lo, Issue issue) {
   constexpr int KS = SliceShape<FMT>::KS;
   constexpr int ns = 128 / KS;
+  // tf32 slices carry 16 values per operand and thread, so all four operands fit the 64-value
+  // prefetch buffer; bf16 slices (32 values) prefetch operands 1-2 and stage 3-4 in the slice.
+  constexpr bool all4 = FMT == kTF32;
   Prefetch pf;
+  float* x3p = pf.x[0] + 16;
+  float* x4p = pf.x[1] + 16;
   fetch_op<FMT>(o1, 0, pf.x[0]);
   fetch_op<FMT>(o2, 0, pf.x[1]);
+  if (all4 && nops > 2) fetch_op<FMT>(o3, 0, x3p);
+  if (all4 && nops > 3) fetch_op<FMT>(o4, 0, x4p);
   for (int s = 0; s < ns; ++s) {
     const int k0 = s * KS;
     store_op<FMT>(t1, o1, lo, pf.x[0]);
     store_op<FMT>(t2, o2, lo, pf.x[1]);
-    if (nops > 2) {
+    if (all4) {
+      if (nops > 2) store_op<FMT>(t3, o3, lo, x3p);
+      if (nops > 3) store_op<FMT>(t4, o4, lo, x4p);
+    } else if (nops > 2) {
       float x3[32], x4[32];
       fetch_op<FMT>(o3, k0, x3);
       if (nops > 3) fetch_op<FMT>(o4, k0, x4);
@@ -438,6 +448,8 @@ __device__ __forceinline__ void kloop_t(MmaBar& mb, const Tile* t1, const Opnd<S
     if (s + 1 < ns) {
       fetch_op<FMT>(o1, k0 + KS, pf.x[0]);
       fetch_op<FMT>(o2, k0 + KS, pf.x[1]);
+      if (all4 && nops > 2) fetch_op<FMT>(o3, k0 + KS, x3p);
+      if (all4 && nops > 3) fetch_op<FMT>(o4, k0 + KS, x4p);
     }
     mbar_wait(mb.bar, mb.phase, mb.status);
     mb.phase ^= 1u;
