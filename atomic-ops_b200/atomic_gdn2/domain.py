@@ -1,10 +1,10 @@
 """Domain of correctness and guards (atomic_gdn2/domain.py:1-62), torch versions.
 
 I-1: g <= 0.   I-2: beta*||k||^2 <= 2.   I-3 (reference BTL diagonal): half_span < 88.
-This build's kernels use one exact reference point per channel and chunk; they need the
-per-channel span of gc = cumsum(g) inside one chunk to stay <= SPAN_LIMIT (128), i.e. a
-half-span <= 64, and flag chunks beyond it (RuntimeError from the operator).  `clamp_g` with
-g_max <= 1 guarantees it for bt = 128.
+This build's kernels rescale each channel of a chunk by one reference point when the channel's
+span of gc = cumsum(g) inside the chunk is <= SPAN_LIMIT (128) and evaluate wider channels'
+intra-chunk terms exactly on the CUDA cores, so every span the reference accepts (g_max up to
+5) is computed; only positive gates (I-1) are refused by the operator.
 """
 from __future__ import annotations
 
@@ -34,8 +34,8 @@ def half_span_from_g(g_hm: torch.Tensor, bt: int, bs2: int) -> float:
 
 
 def chunk_span_max(g_hm: torch.Tensor, bt: int) -> float:
-    """Largest per-channel span (max - min of gc) inside one chunk: the quantity the B200 kernels
-    bound by SPAN_LIMIT."""
+    """Largest per-channel span (max - min of gc) inside one chunk; channels above SPAN_LIMIT take
+    the kernels' exact wide-channel path."""
     b, h, L, d = g_hm.shape
     gc = torch.cumsum(g_hm.float().reshape(b, h, L // bt, bt, d), dim=-2)
     return float((gc.amax(-2) - gc.amin(-2)).max())
@@ -68,7 +68,8 @@ def check_preconditions(g_hm: torch.Tensor, cfg, strict: bool = True) -> dict:
     if strict and status == "STOP":
         raise RuntimeError(f"BTL half_span={hs:.1f} > {BTL_STOP} (limit {BTL_HARD_LIMIT}); reduce bs2 or clamp g")
     span = chunk_span_max(g_hm, cfg.bt)
-    return {"half_span_max": hs, "status": status, "chunk_span_max": span, "kernel_ok": span <= SPAN_LIMIT}
+    return {"half_span_max": hs, "status": status, "chunk_span_max": span, "wide_channels": span > SPAN_LIMIT,
+            "kernel_ok": bool((g_hm <= 0).all())}
 
 
 def safe_bs2_for(g_max: float, candidates=(128, 64, 32, 16, 8)) -> int:

@@ -20,12 +20,14 @@
 // sum_v dh_next[d, v] h_next[d, v] (the derivative through the chunk decay e^gl; it equals the
 // reference's dgc_last + the last-row kg term, mega.py:43-49).  dg is the reverse cumsum of dgc
 // (mega.py:51, B5).
+#include <type_traits>
+
 #include "gdn2_kernels.cuh"
 
 namespace gdn2 {
 
 constexpr uint32_t kPreSmem = 1024 + 6 * 16384 + kT * kGcPitch * 4 + 64;
-constexpr uint32_t kBwdSmem = 1024 + 8 * 16384 + kT * kGcPitch * 4 + 4 * kD * 4 + 64;
+constexpr uint32_t kBwdSmem = 1024 + 8 * 16384 + kT * kGcPitch * 4 + 7 * kD * 4 + 64;
 
 __device__ __forceinline__ uint8_t* align1024b(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
@@ -137,24 +139,86 @@ __global__ void __launch_bounds__(kCT, 1) bwd_pre_kernel(const BwdParams P) {
 }
 
 // ---------------------------------------------------------------------------------------
+// Wide channels (gate span inside the chunk > kSpanMax): exact B4 terms on the CUDA cores.
+// ---------------------------------------------------------------------------------------
+// Row i of  scale dAqk (k e^(gc_i - gc_j))  and  dAkk (k e^(gc_i - gc_j))  for the 16 channels
+// c0..c0+15 (zero for channels that are not wide).  dAqk / dAkk rows come from TMEM (this
+// thread's lane); every thread of the warp runs the same loads.
+template <class TIn>
+__device__ __forceinline__ void wide_dq_dbk(uint32_t S1, uint32_t S2, const TIn* __restrict__ k, const float* gcs,
+                                            const float* wide_s, int i, int c0, float scale, float* oq, float* ob) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j) oq[j] = ob[j] = 0.f;
+#pragma unroll 1
+  for (int jc = 0; jc < kT; jc += 16) {
+    float aq[16], ak[16];
+    tmem_ld16(S1, (uint32_t)jc, aq);
+    tmem_ld16(S2, (uint32_t)jc, ak);
+#pragma unroll 1
+    for (int dd = 0; dd < 16; ++dd) {
+      const int d = c0 + dd;
+      if (wide_s[d] == 0.f) continue;
+      const float gci = gcs[i * kGcPitch + d];
+      float sq = 0.f, sb = 0.f;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int j = jc + e;
+        const float w = (j <= i) ? ld1(k + j * kD + d) * ex(fminf(gci - gcs[j * kGcPitch + d], 0.f)) : 0.f;
+        sq = fmaf(aq[e], w, sq);
+        sb = fmaf(ak[e], w, sb);
+      }
+      oq[dd] += scale * sq;
+      ob[dd] += sb;
+    }
+  }
+}
+// dk contribution of one wide channel d at row j (see step 13 of bwd_intra).
+template <class TIn>
+__device__ __forceinline__ float wide_dk(const float* dqT, const float* dkT, const TIn* __restrict__ q,
+                                         const TIn* __restrict__ k, const TIn* __restrict__ b,
+                                         const float* __restrict__ vnew_g, const float* __restrict__ dhn_g,
+                                         const float* gcs, float gl, int j, int d, float scale) {
+  float tv = 0.f;
+#pragma unroll 4
+  for (int v = 0; v < kD; ++v) tv = fmaf(vnew_g[j * kD + v], dhn_g[d * kD + v], tv);
+  const float gcj = gcs[j * kGcPitch + d];
+  float acc = ex(fminf(gl - gcj, 0.f)) * tv;
+#pragma unroll 4
+  for (int i = 0; i < kT; ++i) {
+    if (i < j) continue;
+    const float e = ex(fminf(gcs[i * kGcPitch + d] - gcj, 0.f));
+    const float bk = ld1(b + i * kD + d) * ld1(k + i * kD + d);
+    const float aq = dqT[j * kT + (i ^ (j & 31))], ak = dkT[j * kT + (i ^ (j & 31))];
+    acc = fmaf((scale * aq * ld1(q + i * kD + d) + ak * bk), e, acc);
+  }
+  return acc;
+}
+
+// ---------------------------------------------------------------------------------------
 // bwd_intra
 // ---------------------------------------------------------------------------------------
-template <class TIn, int B3>
+// WIDE = false handles the chunks without wide channels, WIDE = true the others (flag written by
+// the forward's fwd_intra); each launch returns at once in the other kind of chunk.
+template <class TIn, int B3, bool WIDE>
 __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
   extern __shared__ uint8_t smem_raw[];
   const OpParams& p = P.op;
   uint8_t* sm = align1024b(smem_raw);
   const uint32_t pool = smem_u32(sm);
   float* gcs = reinterpret_cast<float*>(sm + 8 * 16384);
-  float* mid_s = gcs + kT * kGcPitch;
+  float* mid_s = gcs + kT * kGcPitch;  // per-channel reference m (0 for a wide channel)
   float* gl_s = mid_s + kD;
   float* extra_s = gl_s + kD;  // two halves of the last-row decay term
-  uint64_t* bar = reinterpret_cast<uint64_t*>(extra_s + 2 * kD);
+  float* mzE_s = extra_s + 2 * kD;  // m of the zeroed-when-wide E legs (+1e30: wide channel)
+  float* mzF_s = mzE_s + kD;        // m of the F legs (-1e30: wide channel)
+  float* wide_s = mzF_s + kD;       // 1 for a wide channel
+  uint64_t* bar = reinterpret_cast<uint64_t*>(wide_s + kD);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5;
   const int t = crow(), half = chalf(), cb = half * 64;
   const int ch = blockIdx.x, bh = ch / p.NC, c = ch % p.NC;
+  if ((reinterpret_cast<const int*>(p.res + p.rl.wide)[ch] != 0) != WIDE) return;
   const long long off = chunk_off(p, bh, c);
   const TIn* q = reinterpret_cast<const TIn*>(p.q) + off;
   const TIn* k = reinterpret_cast<const TIn*>(p.k) + off;
@@ -192,7 +256,14 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
     float mx, mn;
     bool pos;
     chunk_cumsum(g, gcs, mx, mn, pos);
-    if (tid < kD) mid_s[tid] = 0.5f * (mx + mn);
+    const bool wide = tid < kD && mx - mn > kSpanMax;
+    if (tid < kD) {
+      const float mid = 0.5f * (mx + mn);
+      mid_s[tid] = wide ? 0.f : mid;
+      mzE_s[tid] = wide ? 1e30f : mid;
+      mzF_s[tid] = wide ? -1e30f : mid;
+      wide_s[tid] = wide ? 1.f : 0.f;
+    }
   }
   {
     // last-row decay term: sum_v dh_next[d, v] h_next[d, v] for channel d = t (two column halves)
@@ -237,7 +308,7 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
   };
   auto src_dhn_gl = [&](int r, int c0, float* x) {  // row d = r of e^(gl-m) dh_next
     ld4_f(dhn_g + r * kD + c0, x);
-    const float s = ex(gl_s[r] - mid_s[r]);
+    const float s = ex(gl_s[r] - mzE_s[r]);
 #pragma unroll
     for (int j = 0; j < 4; ++j) x[j] *= s;
   };
@@ -249,17 +320,25 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) x[j] = x[j] * kv[j] * ex(gr[j] - mid_s[c0 + j]);
   };
-  auto src_qE = [&](int r, int c0, float* x) {
+  auto src_bkEz = [&](int r, int c0, float* x) {  // b k E, zero in wide channels (B4 operand)
+    float kv[4];
+    ld4_in(b + r * kD + c0, x);
+    ld4_in(k + r * kD + c0, kv);
+    const float* gr = gcrow(r) + c0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) x[j] = x[j] * kv[j] * ex(gr[j] - mzE_s[c0 + j]);
+  };
+  auto src_qE = [&](int r, int c0, float* x) {  // scale q E, zero in wide channels
     ld4_in(q + r * kD + c0, x);
     const float* gr = gcrow(r) + c0;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) x[j] = scale * x[j] * ex(gr[j] - mid_s[c0 + j]);
+    for (int j = 0; j < 4; ++j) x[j] = scale * x[j] * ex(gr[j] - mzE_s[c0 + j]);
   };
-  auto src_kF = [&](int r, int c0, float* x) {
+  auto src_kF = [&](int r, int c0, float* x) {  // k F, zero in wide channels
     ld4_in(k + r * kD + c0, x);
     const float* gr = gcrow(r) + c0;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) x[j] = x[j] * ex(mid_s[c0 + j] - gr[j]);
+    for (int j = 0; j < 4; ++j) x[j] = x[j] * ex(mzF_s[c0 + j] - gr[j]);
   };
   auto src_wv = [&](int r, int c0, float* x) {
     float vv[4];
@@ -379,43 +458,50 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
   // 9. S3 = scale do (e^m h_pre)^T (B3)  +  scale dAqk (k F) (B4)
   gemm1(m3, pool, mb, S3, kany(src_do_s), kany(src_hpre_em), false, false);
   gemm1(mh, pool, mb, S3, kmaj(tm_scaled(S1)), mn_any(src_kF), false, true);
-  // 10.-11. finish dq and db;  S3 <- dgc partial;  S0 <- Dbk b E (pre-scaled dk partial)
-  {
+  // 10.-11. finish dq and db;  S3 <- dgc partial;  S0 <- Dbk b E (pre-scaled dk partial).
+  //     Wide channels (m = 0): their B4 terms were left out of the products above and are added
+  //     exactly here, and S0 keeps Dbk b (their dk is finished without the F leg in step 13).
+  auto ep1011 = [&](auto wide_tag) {
+    constexpr bool kWide = decltype(wide_tag)::value;
     const float* gr = gcrow(t);
     float* xb = xbuf(sm);
 #pragma unroll 1
     for (int hh = 0; hh < 2; ++hh) {
       float q2[32], k2[32], b2[32];
-  #pragma unroll
+#pragma unroll
       for (int j = 0; j < 2; ++j) {
         ld16_in(q + t * kD + cb + 32 * hh + 16 * j, q2 + 16 * j);
         ld16_in(k + t * kD + cb + 32 * hh + 16 * j, k2 + 16 * j);
         ld16_in(b + t * kD + cb + 32 * hh + 16 * j, b2 + 16 * j);
       }
-  #pragma unroll
+#pragma unroll
       for (int jj = 0; jj < 2; ++jj) {
         const int c0 = cb + 32 * hh + 16 * jj;
         const float* qv = q2 + 16 * jj;
         const float* kv = k2 + 16 * jj;
         const float* bv = b2 + 16 * jj;
-        float x[16], y[16], E[16], dgcp[16];
-  #pragma unroll
+        float x[16], y[16], E[16], dgcp[16], wq[16], wb[16];
+        if constexpr (kWide) wide_dq_dbk(S1, S2, k, gcs, wide_s, t, c0, scale, wq, wb);
+#pragma unroll
         for (int j = 0; j < 16; ++j) E[j] = ex(gr[c0 + j] - mid_s[c0 + j]);
         tmem_ld16(S3, c0, x);  // Dq / E
-  #pragma unroll
+#pragma unroll
         for (int j = 0; j < 16; ++j) {
           x[j] *= E[j];
+          if constexpr (kWide) x[j] += wq[j];
           y[j] = sanitize(x[j], clip);
           dgcp[j] = qv[j] * x[j];
         }
         xb2_put16(xb, 0, 16 * jj, y);
         tmem_ld16(S0, c0, x);  // Dbk / E
-  #pragma unroll
+#pragma unroll
         for (int j = 0; j < 16; ++j) {
           x[j] *= E[j];
+          if constexpr (kWide) x[j] += wb[j];
           y[j] = sanitize(x[j] * kv[j], clip);
           dgcp[j] += 2.f * bv[j] * kv[j] * x[j];
-          x[j] = x[j] * bv[j] * E[j];
+          if constexpr (kWide) x[j] = x[j] * bv[j] * (wide_s[c0 + j] != 0.f ? 1.f : E[j]);
+          else x[j] = x[j] * bv[j] * E[j];
         }
         xb2_put16(xb, 1, 16 * jj, y);
         tmem_st16(S3, c0, dgcp);
@@ -424,15 +510,16 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
       xb2_flush(xb, 0, dq, kD, cb + 32 * hh);
       xb2_flush(xb, 1, db, kD, cb + 32 * hh);
     }
-  }
+  };
+  ep1011(std::integral_constant<bool, WIDE>{});
   sync_all();
   // 12. S0 += v_new (e^(gl-m) dh_next)^T (B3)  +  scale dAqk^T (q E) + dAkk^T (bk E) (B4)
   gemm1(m3, pool, mb, S0, kany(src_vnew), kany(src_dhn_gl), false, true);
-  gemm2(mh, pool, mb, S0, mn_own(tm(S1)), mn_any(src_qE), false, true, S0, mn_own(tm(S2)), mn_any(src_bkE), false,
+  gemm2(mh, pool, mb, S0, mn_own(tm(S1)), mn_any(src_qE), false, true, S0, mn_own(tm(S2)), mn_any(src_bkEz), false,
         true, false, false);
   // 13. dk = F o S0;  dgc = S3 - k o dk (+ decay term on the last row).  dgc overwrites this
   //     thread's own half-row of gcs (no other thread reads that row any more).
-  {
+  if constexpr (!WIDE) {
     float* gr = gcs + t * kGcPitch;
     float k4[64];
 #pragma unroll
@@ -456,8 +543,58 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
       for (int j = 0; j < 16; ++j) gr[c0 + j] = dgcp[j];
     }
     xb_flush(xbuf(sm), dk, kD, cb);
+  } else {
+    // Wide channels: dk[j,d] = (Dbk b)[j,d] + e^(gl-gc[j,d]) (v_new dh_next^T)[j,d]
+    //   + sum_{i>=j} (scale dAqk[i,j] q[i,d] + dAkk[i,j] (b k)[i,d]) e^(gc[i,d]-gc[j,d]),
+    // with dAqk / dAkk read by column from transposed copies in the (idle) operand pool.
+    float* dqT = reinterpret_cast<float*>(sm);
+    float* dkT = dqT + kT * kT;
+#pragma unroll 1
+    for (int c0 = cb; c0 < cb + 64; c0 += 16) {
+      float a1[16], a2[16];
+      tmem_ld16(S1, c0, a1);
+      tmem_ld16(S2, c0, a2);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int col = c0 + j;
+        dqT[col * kT + (t ^ (col & 31))] = a1[j];
+        dkT[col * kT + (t ^ (col & 31))] = a2[j];
+      }
+    }
+    __syncthreads();
+    const float* gr = gcs + t * kGcPitch;
+    float dgc_keep[64];
+#pragma unroll 1
+    for (int jj = 0; jj < 4; ++jj) {
+      const int c0 = cb + 16 * jj;
+      float x[16], y[16], dgcp[16], kv[16];
+      ld16_in(k + t * kD + c0, kv);
+      tmem_ld16(S0, c0, x);
+      tmem_ld16(S3, c0, dgcp);
+#pragma unroll 1
+      for (int j = 0; j < 16; ++j) {
+        const int d = c0 + j;
+        if (wide_s[d] != 0.f) {
+          x[j] += wide_dk(dqT, dkT, q, k, b, vnew_g, dhn_g, gcs, gl_s[d], t, d, scale);
+        } else {
+          x[j] *= ex(mid_s[d] - gr[d]);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        y[j] = sanitize(x[j], clip);
+        dgcp[j] -= kv[j] * x[j];
+        if (t == kT - 1) dgcp[j] += extra_s[c0 + j] + extra_s[kD + c0 + j];
+        dgc_keep[16 * jj + j] = dgcp[j];
+      }
+      st16_out(dk + t * kD + c0, y);
+    }
+    __syncthreads();  // every thread has read all of gcs; dgc may now overwrite it
+    float* gw = gcs + t * kGcPitch;
+#pragma unroll
+    for (int j = 0; j < 64; ++j) gw[cb + j] = dgc_keep[j];
   }
-  __syncthreads();
+  __syncthreads();  // all rows of dgc are in gcs
   // 14. dg = reverse cumsum of dgc over the chunk (B5)
   if (tid < kD) {
     float acc = 0.f;
@@ -478,18 +615,18 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
 
 template <class TIn, int B3>
 static cudaError_t launch_bwd_pre_t(const BwdParams& p, int nblocks, cudaStream_t st) {
-  cudaError_t e =
-      cudaFuncSetAttribute(bwd_pre_kernel<TIn, B3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPreSmem);
+  static unsigned long long done = 0;
+  cudaError_t e = smem_attr_once(bwd_pre_kernel<TIn, B3>, (int)kPreSmem, done);
   if (e != cudaSuccess) return e;
   bwd_pre_kernel<TIn, B3><<<nblocks, kCT, kPreSmem, st>>>(p);
   return cudaGetLastError();
 }
-template <class TIn, int B3>
+template <class TIn, int B3, bool WIDE>
 static cudaError_t launch_bwd_intra_t(const BwdParams& p, int nblocks, cudaStream_t st) {
-  cudaError_t e =
-      cudaFuncSetAttribute(bwd_intra_kernel<TIn, B3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBwdSmem);
+  static unsigned long long done = 0;
+  cudaError_t e = smem_attr_once(bwd_intra_kernel<TIn, B3, WIDE>, (int)kBwdSmem, done);
   if (e != cudaSuccess) return e;
-  bwd_intra_kernel<TIn, B3><<<nblocks, kCT, kBwdSmem, st>>>(p);
+  bwd_intra_kernel<TIn, B3, WIDE><<<nblocks, kCT, kBwdSmem, st>>>(p);
   return cudaGetLastError();
 }
 // Compile-time precision for the reference's default B3 mode (bf16x3) and the all-bf16 mode.
@@ -501,9 +638,12 @@ static cudaError_t launch_bwd_pre_m(const BwdParams& p, int nblocks, cudaStream_
 }
 template <class TIn>
 static cudaError_t launch_bwd_intra_m(const BwdParams& p, int nblocks, cudaStream_t st) {
-  if (p.op.b3_mode == GDN2_PREC_BF16X3) return launch_bwd_intra_t<TIn, GDN2_PREC_BF16X3>(p, nblocks, st);
-  if (p.op.b3_mode == GDN2_PREC_DEFAULT) return launch_bwd_intra_t<TIn, GDN2_PREC_DEFAULT>(p, nblocks, st);
-  return launch_bwd_intra_t<TIn, -1>(p, nblocks, st);
+  cudaError_t e;
+  if (p.op.b3_mode == GDN2_PREC_BF16X3) e = launch_bwd_intra_t<TIn, GDN2_PREC_BF16X3, false>(p, nblocks, st);
+  else if (p.op.b3_mode == GDN2_PREC_DEFAULT) e = launch_bwd_intra_t<TIn, GDN2_PREC_DEFAULT, false>(p, nblocks, st);
+  else e = launch_bwd_intra_t<TIn, -1, false>(p, nblocks, st);
+  if (e != cudaSuccess) return e;
+  return launch_bwd_intra_t<TIn, -1, true>(p, nblocks, st);  // chunks with wide channels
 }
 
 cudaError_t launch_bwd_pre(const BwdParams& p, bool bf16, int nblocks, cudaStream_t st) {

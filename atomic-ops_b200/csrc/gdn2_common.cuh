@@ -102,6 +102,8 @@ __device__ __forceinline__ void ld4(const __nv_bfloat16* p, float v[4]) {
   float2 fa = __bfloat1622float2(a), fb = __bfloat1622float2(b);
   v[0] = fa.x; v[1] = fa.y; v[2] = fb.x; v[3] = fb.y;
 }
+__device__ __forceinline__ float ld1(const float* p) { return __ldg(p); }
+__device__ __forceinline__ float ld1(const __nv_bfloat16* p) { return __bfloat162float(*p); }
 __device__ __forceinline__ void st4(float* p, const float v[4]) {
   *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
 }
@@ -257,6 +259,21 @@ __device__ __forceinline__ void tmem_st32(uint32_t tbase, uint32_t col, const fl
       "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Raise a kernel's dynamic shared-memory limit once per device (the attribute persists), so that
+// launches made while a stream is being captured into a CUDA graph issue no attribute calls.
+// `done` is a per-kernel bit mask of devices already set up.
+template <class Kernel>
+inline cudaError_t smem_attr_once(Kernel kernel, int bytes, unsigned long long& done) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (done & bit) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done |= bit;
+  return e;
 }
 
 // ---------------------------------------------------------------------------

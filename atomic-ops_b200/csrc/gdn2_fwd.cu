@@ -14,16 +14,21 @@
 // Akk[i,j] = sum_d b[i,d] k[i,d] k[j,d] e^(gc[i,d]-gc[j,d]) (i > j) are computed as plain
 // 128x128x128 tensor-core products of rescaled operands q e^(gc-m), k e^(m-gc) with one
 // reference point per channel, m = (max_t gc + min_t gc) / 2.  Every leg then lies in
-// [e^(-span/2), e^(span/2)]; chunks whose span exceeds kSpanMax are flagged
-// (GDN2_DEV_SPAN).  This is the balanced-leg idea of the reference's BTL diagonal
+// [e^(-span/2), e^(span/2)].  This is the balanced-leg idea of the reference's BTL diagonal
 // (fwd/scores.py:16-28) applied to the whole chunk, which the B200's fp32 range allows for
-// the spans the operator meets in practice.
+// spans up to kSpanMax.  Channels whose span inside the chunk is larger ("wide" channels,
+// strongly decaying gates) are left out of the tensor-core products (their legs are zero) and
+// their contribution sum_d q[i,d] k[j,d] e^(gc[i,d]-gc[j,d]) is added exactly by the CUDA
+// cores, with the exponent difference formed first (<= 0 on the causal entries); chunks
+// without wide channels never run that code.
 //
 // WY inverse.  With N = I + Se (Se = (1-eps) Akk, strictly lower), Dg its four 32x32 diagonal
 // blocks and R the strictly block-lower rest, N^-1 = (I - W)(I + W^2) Dg^-1 with W = Dg^-1 R
 // (W^4 = 0).  Dg^-1 comes from warp-level forward substitution (one warp per block, lane =
 // column, fp32); the four remaining products run on the tensor core in solve_dot_mode.  This
 // replaces the reference's leaf + block-doubling ladder (fwd/solve.py:9-43).
+#include <type_traits>
+
 #include "gdn2_kernels.cuh"
 
 namespace gdn2 {
@@ -31,7 +36,7 @@ namespace gdn2 {
 constexpr uint32_t kPoolBytes = 6 * 16384;                  // six 16 KB operand tiles
 constexpr uint32_t kGcBytes = kT * kGcPitch * 4;             // 67,584
 constexpr uint32_t kDsmFloats = 4 * 32 * 33;                 // four padded 32x32 blocks
-constexpr uint32_t kIntraSmem = 1024 + kPoolBytes + kGcBytes + kDsmFloats * 4 + 2 * kD * 4 + 64;
+constexpr uint32_t kIntraSmem = 1024 + kPoolBytes + kGcBytes + kDsmFloats * 4 + 4 * kD * 4 + 64;
 constexpr uint32_t kOutSmem = 1024 + kPoolBytes + kGcBytes + 64;
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
@@ -41,16 +46,44 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
 // ---------------------------------------------------------------------------------------
 // fwd_intra
 // ---------------------------------------------------------------------------------------
-template <class TIn, int DOT, int SOLVE>
+// Wide channels' exact contribution to row i of the raw scores, columns j = c0..c0+15:
+//   aq[j] += sum_{d wide} q[i,d] k[j,d] e^(gc[i,d]-gc[j,d]),  ak[j] = sum_{d wide} (b k)[i,d] k[j,d] e^(...)
+// (entries with j > i are masked by the caller; their exponent is clamped at 0).
+template <class TIn>
+__device__ __forceinline__ void wide_scores(const TIn* __restrict__ q, const TIn* __restrict__ k,
+                                            const TIn* __restrict__ b, const float* gcs, const float* wide_s, int i,
+                                            int c0, float* aq, float* ak) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j) ak[j] = 0.f;
+#pragma unroll 1
+  for (int d = 0; d < kD; ++d) {
+    if (wide_s[d] == 0.f) continue;
+    const float gci = gcs[i * kGcPitch + d];
+    const float qi = ld1(q + i * kD + d), bki = ld1(b + i * kD + d) * ld1(k + i * kD + d);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int jj = c0 + j;
+      const float w = ld1(k + jj * kD + d) * ex(fminf(gci - gcs[jj * kGcPitch + d], 0.f));
+      aq[j] = fmaf(qi, w, aq[j]);
+      ak[j] = fmaf(bki, w, ak[j]);
+    }
+  }
+}
+
+// WIDE = false: the fast kernel; it records in the residual whether the chunk has wide channels
+// and leaves such chunks to the WIDE = true launch that follows it (which skips all others).
+template <class TIn, int DOT, int SOLVE, bool WIDE>
 __global__ void __launch_bounds__(kCT, 1) fwd_intra_kernel(const OpParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
   const uint32_t pool = smem_u32(sm);
   float* gcs = reinterpret_cast<float*>(sm + kPoolBytes);
   float* dsm = reinterpret_cast<float*>(sm + kPoolBytes + kGcBytes);
-  float* mid_s = dsm + kDsmFloats;
-  float* gl_s = mid_s + kD;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(gl_s + kD);
+  float* mzE_s = dsm + kDsmFloats;  // per-channel reference m of the E legs (+1e30: wide channel)
+  float* gl_s = mzE_s + kD;
+  float* mzF_s = gl_s + kD;          // reference of the F legs (-1e30: wide channel)
+  float* wide_s = mzF_s + kD;        // 1 for a wide channel
+  uint64_t* bar = reinterpret_cast<uint64_t*>(wide_s + kD);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -76,6 +109,28 @@ __global__ void __launch_bounds__(kCT, 1) fwd_intra_kernel(const OpParams p) {
   const Mode ms = mode_from_enum(SOLVE >= 0 ? SOLVE : p.solve_mode);
   const float clip = p.clip;
 
+  int* wide_flag = reinterpret_cast<int*>(p.res + p.rl.wide) + ch;
+  if constexpr (WIDE) {
+    if (*wide_flag == 0) return;
+  }
+  {
+    float mx, mn;
+    bool pos;
+    chunk_cumsum(g, gcs, mx, mn, pos);
+    if (tid < kD) {
+      const bool wide = mx - mn > kSpanMax;
+      const float mid = 0.5f * (mx + mn);
+      mzE_s[tid] = wide ? 1e30f : mid;
+      mzF_s[tid] = wide ? -1e30f : mid;
+      wide_s[tid] = wide ? 1.f : 0.f;
+      if (pos && !WIDE) atomicOr(p.status, kStatusPositiveGate);
+    }
+    const int any_wide = __syncthreads_or(tid < kD && mx - mn > kSpanMax);
+    if constexpr (!WIDE) {
+      if (tid == 0) *wide_flag = any_wide;
+      if (any_wide) return;
+    }
+  }
   if (warp == 0) {
     tmem_alloc(tslot, 512);
     tmem_relinquish();
@@ -83,16 +138,6 @@ __global__ void __launch_bounds__(kCT, 1) fwd_intra_kernel(const OpParams p) {
   if (tid == 0) {
     mbar_init(bar, 1);
     fence_mbar_init();
-  }
-  {
-    float mx, mn;
-    bool pos;
-    chunk_cumsum(g, gcs, mx, mn, pos);
-    if (tid < kD) {
-      mid_s[tid] = 0.5f * (mx + mn);
-      if (pos) atomicOr(p.status, kStatusPositiveGate);
-      if (mx - mn > kSpanMax) atomicOr(p.status, kStatusSpan);
-    }
   }
   tc_fence_before();
   __syncthreads();
@@ -108,7 +153,7 @@ __global__ void __launch_bounds__(kCT, 1) fwd_intra_kernel(const OpParams p) {
     ld4_in(q + r * kD + c0, x);
     const float* gr = gcs + r * kGcPitch + c0;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) x[j] *= ex(gr[j] - mid_s[c0 + j]);
+    for (int j = 0; j < 4; ++j) x[j] *= ex(gr[j] - mzE_s[c0 + j]);
   };
   auto src_bkE = [&](int r, int c0, float* x) {  // b k e^(gc - m)
     float kv[4];
@@ -116,13 +161,13 @@ __global__ void __launch_bounds__(kCT, 1) fwd_intra_kernel(const OpParams p) {
     ld4_in(k + r * kD + c0, kv);
     const float* gr = gcs + r * kGcPitch + c0;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) x[j] = x[j] * kv[j] * ex(gr[j] - mid_s[c0 + j]);
+    for (int j = 0; j < 4; ++j) x[j] = x[j] * kv[j] * ex(gr[j] - mzE_s[c0 + j]);
   };
   auto src_kF = [&](int r, int c0, float* x) {  // k e^(m - gc)
     ld4_in(k + r * kD + c0, x);
     const float* gr = gcs + r * kGcPitch + c0;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) x[j] *= ex(mid_s[c0 + j] - gr[j]);
+    for (int j = 0; j < 4; ++j) x[j] *= ex(mzF_s[c0 + j] - gr[j]);
   };
   auto src_kb = [&](int r, int c0, float* x) {  // b k e^min(gc, 0)
     float kv[4];
@@ -175,17 +220,24 @@ __global__ void __launch_bounds__(kCT, 1) fwd_intra_kernel(const OpParams p) {
         false, false, true);
 
   // ---- 2. Aqk out (scale, causal, sanitize); Se = (1-eps) sanitize(Akk) strict, in place -----------
-  {
+  // (the body is instantiated twice: chunks with wide channels add their exact terms)
+  auto ep2 = [&](auto wide_tag) {
+    constexpr bool kWide = decltype(wide_tag)::value;
     const float keep = 1.0f - p.eps;
     const int blk = t >> 5;
     float* xb = xbuf(sm);
     for (int c0 = cb; c0 < cb + 64; c0 += 16) {
-      float x[16];
+      float x[16], wk[16];
       tmem_ld16(S0, c0, x);
+      if constexpr (kWide) wide_scores(q, k, b, gcs, wide_s, t, c0, x, wk);
 #pragma unroll
       for (int j = 0; j < 16; ++j) x[j] = (c0 + j <= t) ? sanitize(p.scale * x[j], clip) : 0.f;
       xb_put16(xb, c0 - cb, x);
       tmem_ld16(S1, c0, x);
+      if constexpr (kWide) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) x[j] += wk[j];
+      }
 #pragma unroll
       for (int j = 0; j < 16; ++j) x[j] = (c0 + j < t) ? keep * sanitize(x[j], clip) : 0.f;
       tmem_st16(S1, c0, x);
@@ -195,7 +247,8 @@ __global__ void __launch_bounds__(kCT, 1) fwd_intra_kernel(const OpParams p) {
       }
     }
     xb_flush(xb, aqk_g, kT, cb);
-  }
+  };
+  ep2(std::integral_constant<bool, WIDE>{});
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -403,29 +456,35 @@ __global__ void __launch_bounds__(kCT, 1) fwd_out_kernel(const OpParams p, float
 // ---------------------------------------------------------------------------------------
 // Kernels are compiled with compile-time precision modes for the configurations that matter
 // (the reference's defaults and the all-bf16 mode), and with runtime modes for the rest (-1).
-template <class TIn, int DOT, int SOLVE>
+template <class TIn, int DOT, int SOLVE, bool WIDE>
 static cudaError_t launch_fwd_intra_t(const OpParams& p, int nblocks, cudaStream_t st) {
-  cudaError_t e = cudaFuncSetAttribute(fwd_intra_kernel<TIn, DOT, SOLVE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)kIntraSmem);
+  static unsigned long long done = 0;
+  cudaError_t e = smem_attr_once(fwd_intra_kernel<TIn, DOT, SOLVE, WIDE>, (int)kIntraSmem, done);
   if (e != cudaSuccess) return e;
-  fwd_intra_kernel<TIn, DOT, SOLVE><<<nblocks, kCT, kIntraSmem, st>>>(p);
+  fwd_intra_kernel<TIn, DOT, SOLVE, WIDE><<<nblocks, kCT, kIntraSmem, st>>>(p);
   return cudaGetLastError();
 }
 template <class TIn, int DOT>
 static cudaError_t launch_fwd_out_t(const OpParams& p, float* o, int nblocks, cudaStream_t st) {
-  cudaError_t e = cudaFuncSetAttribute(fwd_out_kernel<TIn, DOT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)kOutSmem);
+  static unsigned long long done = 0;
+  cudaError_t e = smem_attr_once(fwd_out_kernel<TIn, DOT>, (int)kOutSmem, done);
   if (e != cudaSuccess) return e;
   fwd_out_kernel<TIn, DOT><<<nblocks, kCT, kOutSmem, st>>>(p, o);
   return cudaGetLastError();
 }
+// The fast launch, then the launch for chunks with wide channels (runtime modes; it returns at
+// once in every other chunk).
 template <class TIn>
 static cudaError_t launch_fwd_intra_m(const OpParams& p, int nblocks, cudaStream_t st) {
+  cudaError_t e;
   if (p.dot_mode == GDN2_PREC_HIGHEST && p.solve_mode == GDN2_PREC_BF16X3)
-    return launch_fwd_intra_t<TIn, GDN2_PREC_HIGHEST, GDN2_PREC_BF16X3>(p, nblocks, st);
-  if (p.dot_mode == GDN2_PREC_DEFAULT && p.solve_mode == GDN2_PREC_DEFAULT)
-    return launch_fwd_intra_t<TIn, GDN2_PREC_DEFAULT, GDN2_PREC_DEFAULT>(p, nblocks, st);
-  return launch_fwd_intra_t<TIn, -1, -1>(p, nblocks, st);
+    e = launch_fwd_intra_t<TIn, GDN2_PREC_HIGHEST, GDN2_PREC_BF16X3, false>(p, nblocks, st);
+  else if (p.dot_mode == GDN2_PREC_DEFAULT && p.solve_mode == GDN2_PREC_DEFAULT)
+    e = launch_fwd_intra_t<TIn, GDN2_PREC_DEFAULT, GDN2_PREC_DEFAULT, false>(p, nblocks, st);
+  else
+    e = launch_fwd_intra_t<TIn, -1, -1, false>(p, nblocks, st);
+  if (e != cudaSuccess) return e;
+  return launch_fwd_intra_t<TIn, -1, -1, true>(p, nblocks, st);
 }
 template <class TIn>
 static cudaError_t launch_fwd_out_m(const OpParams& p, float* o, int nblocks, cudaStream_t st) {

@@ -17,7 +17,7 @@ __host__ __device__ inline uint32_t image_bytes(Mode m) { return image_part_byte
 
 // Per-call residual layout (byte offsets from the residual base), all regions 256-byte aligned.
 struct ResLayout {
-  size_t aqk, ainv, wp, u, mf, bc, hs, vnew, total;
+  size_t aqk, ainv, wp, u, mf, bc, hs, vnew, wide, total;
   uint32_t mf_stride;  // bytes per chunk-head of the forward state-transition image
 };
 
@@ -37,6 +37,7 @@ __host__ __device__ inline ResLayout res_layout(int BH, int NC, Mode fwd_scan) {
   r.bc = o; o = align256(o + nch * mat);
   r.hs = o; o = align256(o + (size_t)BH * (NC + 1) * mat);  // h entering each chunk, then h_final
   r.vnew = o; o = align256(o + nch * mat);
+  r.wide = o; o = align256(o + nch * sizeof(int));  // per chunk-head: 1 if it has wide channels
   r.total = o;
   return r;
 }

@@ -139,7 +139,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanParams sp) 
 }
 
 cudaError_t launch_scan(const ScanParams& sp, int BH, cudaStream_t st) {
-  cudaError_t e = cudaFuncSetAttribute(scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kScanSmem);
+  static unsigned long long done = 0;
+  cudaError_t e = smem_attr_once(scan_kernel, (int)kScanSmem, done);
   if (e != cudaSuccess) return e;
   scan_kernel<<<BH * (kD / kDV), kThreads, kScanSmem, st>>>(sp);
   return cudaGetLastError();

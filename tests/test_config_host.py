@@ -137,7 +137,9 @@ def test_domain_stats():
     r = domain.check_preconditions(g, make_cfg(), strict=False)
     assert abs(r["half_span_max"] - 0.5 * 31 * 0.5) < 1e-4
     assert abs(r["chunk_span_max"] - 127 * 0.5) < 1e-3 and r["kernel_ok"]
-    assert not domain.check_preconditions(-torch.full((1, 1, 128, 8), 1.5), make_cfg(), strict=False)["kernel_ok"]
+    wide = domain.check_preconditions(-torch.full((1, 1, 128, 8), 1.5), make_cfg(), strict=False)
+    assert wide["wide_channels"] and wide["kernel_ok"]
+    assert not domain.check_preconditions(torch.full((1, 1, 128, 8), 0.1), make_cfg(), strict=False)["kernel_ok"]
     assert domain.clamp_g(torch.tensor([-7.0, -1.0]), 5.0).tolist() == [-5.0, -1.0]
     assert abs(torch.nn.functional.softplus(torch.tensor(domain.init_g_bias(0.05))).item() - 0.05) < 1e-6
     assert domain.safe_bs2_for(5.0) == 16

@@ -100,8 +100,8 @@ def test_bf16_inputs_fp32_products():
 
 
 @pytest.mark.parametrize("name,seed,g,k,b", [
-    ("benign0", 0, 0.05, 1.0, 0.5), ("benign1", 1, 0.05, 1.0, 0.5), ("near_zero", 3, 0.001, 1.0, 0.5),
-    ("b_near_one", 5, 0.3, 1.0, 0.95), ("large_k_stable", 4, 0.3, 8.0, 0.02)])
+    ("benign0", 0, 0.05, 1.0, 0.5), ("benign1", 1, 0.05, 1.0, 0.5), ("strong_decay", 2, 3.0, 1.0, 0.5),
+    ("near_zero", 3, 0.001, 1.0, 0.5), ("b_near_one", 5, 0.3, 1.0, 0.95), ("large_k_stable", 4, 0.3, 8.0, 0.02)])
 def test_reference_fixture_regimes(name, seed, g, k, b):
     """The reference's in-domain regimes (tests_gdn2/conftest.py:6-11) at D=128, damped WY
     (wy_eps=1e-3, the default), non-zero h0, arbitrary cotangents."""
@@ -209,16 +209,21 @@ def test_long_sequence_segments_vs_oracle():
     _compare(_run_op(cfg, xs, h0), _run_oracle(cfg.with_(max_chunks_per_call=32), xs, h0), 1e-4)
 
 
-def test_out_of_range_gate_span_raises():
-    """Chunks whose per-channel gate span exceeds the supported range are flagged by the kernel
-    and raised on the host (never silently wrong); the reference's own BTL path would return
-    garbage past its limit (domain.py:1-6, bug T-22)."""
+@pytest.mark.parametrize("g_wide", [-1.5, -5.0])
+def test_wide_gate_spans_match_oracle(g_wide):
+    """Channels whose gate span inside a chunk exceeds the single-reference range (here
+    128 x 1.5 = 192 and 128 x 5 = 640, up to the reference's g_max of 5) next to ordinary
+    channels: their terms are evaluated exactly on the CUDA cores; o, h_final and all gradients
+    (and dh0) against the oracle."""
     cfg = make_cfg()
-    xs, h0 = O.bench_inputs(1, 1, 256, D, 0)
+    xs, h0 = O.bench_inputs(1, 2, 256, D, 0)
     xs = list(xs)
-    xs[5] = torch.full_like(xs[5], -1.5)  # 128 tokens * 1.5 = 190 > 128
-    with pytest.raises(RuntimeError, match="span"):
-        make_blr_trainable(cfg, 0.1)(*(t.cuda() for t in xs))
+    g = xs[5].clone()
+    gen = torch.Generator().manual_seed(1)
+    wide = torch.rand(D, generator=gen) < 0.25
+    g[..., wide] = g_wide * (0.8 + 0.4 * torch.rand(g[..., wide].shape, generator=gen))
+    xs[5] = g
+    _compare(_run_op(cfg, xs, h0), _run_oracle(cfg, xs, h0), 1e-4)
 
 
 def test_positive_gate_raises():
