@@ -266,16 +266,31 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
     }
   }
   {
-    // last-row decay term: sum_v dh_next[d, v] h_next[d, v] for channel d = t (two column halves)
-    float acc = 0.f;
-    for (int c0 = cb; c0 < cb + 64; c0 += 16) {
-      float a[16], h[16];
-      ld16_f(dhn_g + t * kD + c0, a);
-      ld16_f(hnext_g + t * kD + c0, h);
+    // last-row decay term: sum_v dh_next[d, v] h_next[d, v] per channel d, one warp per row
+    // (lane l reads columns 4l .. 4l+3: coalesced 512-byte row reads), stored in extra_s[d]
+    // (extra_s[kD + d] stays 0).
+    const int lane = tid & 31;
+    float part[16];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) acc = fmaf(a[j], h[j], acc);
+    for (int i = 0; i < 16; ++i) {
+      const int d = warp * 16 + i;
+      float a[4], h[4];
+      ld4_f(dhn_g + d * kD + 4 * lane, a);
+      ld4_f(hnext_g + d * kD + 4 * lane, h);
+      part[i] = a[0] * h[0] + a[1] * h[1] + a[2] * h[2] + a[3] * h[3];
     }
-    extra_s[half * kD + t] = acc;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) part[i] += __shfl_xor_sync(0xffffffffu, part[i], o);
+    }
+    if (lane < 16) {
+      float v = part[0];
+#pragma unroll
+      for (int i = 1; i < 16; ++i) v = (lane == i) ? part[i] : v;
+      extra_s[warp * 16 + lane] = v;
+      extra_s[kD + warp * 16 + lane] = 0.f;
+    }
   }
   tc_fence_before();
   __syncthreads();
