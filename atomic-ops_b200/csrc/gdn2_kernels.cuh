@@ -396,45 +396,48 @@ __device__ __forceinline__ void stage_own(const Tile tt[2], const Opnd<Src>& op,
   }
 }
 
-// Register buffer for the prefetched slice of operands 1-2.
-struct Prefetch {
-  float x[2][32];
-};
-
 // One K-loop of up to four operands (ops 1-2: pair 1's A and B, or A1 and the shared B; ops 3-4:
-// the rest).  Software-pipelined: the global / shared loads of ops 1-2 for slice s+1 are issued
-// right after slice s's MMAs, so their latency overlaps the tensor core; TMEM-backed MN-major
-// operands are staged in the slice itself (TMEM loads are short).
+// the rest).  Software-pipelined: the global loads of the next slice are issued right after a
+// slice's MMAs, so their latency overlaps the tensor core.  A 64-value register buffer holds the
+// prefetched slices of the first global operands (two for bf16 slices, four for tf32); TMEM- and
+// shared-memory-backed operands, and global ones beyond the buffer, are staged inside the slice.
 template <int FMT, class S1, class S2, class S3, class S4, class Issue>
 __device__ __forceinline__ void kloop_t(MmaBar& mb, const Tile* t1, const Opnd<S1>& o1, const Tile* t2,
                                         const Opnd<S2>& o2, const Tile* t3, const Opnd<S3>& o3, const Tile* t4,
                                         const Opnd<S4>& o4, int nops, bool lo, Issue issue) {
   constexpr int KS = SliceShape<FMT>::KS;
   constexpr int ns = 128 / KS;
-  // tf32 slices carry 16 values per operand and thread, so all four operands fit the 64-value
-  // prefetch buffer; bf16 slices (32 values) prefetch operands 1-2 and stage 3-4 in the slice.
-  constexpr bool all4 = FMT == kTF32;
-  Prefetch pf;
-  float* x3p = pf.x[0] + 16;
-  float* x4p = pf.x[1] + 16;
-  fetch_op<FMT>(o1, 0, pf.x[0]);
-  fetch_op<FMT>(o2, 0, pf.x[1]);
-  if (all4 && nops > 2) fetch_op<FMT>(o3, 0, x3p);
-  if (all4 && nops > 3) fetch_op<FMT>(o4, 0, x4p);
+  constexpr int SLOT = FMT == kTF32 ? 16 : 32;  // values per operand slice and thread
+  constexpr int NSLOT = 64 / SLOT;
+  auto glob = [](int kind) { return kind == kKAny || kind == kMnAny; };
+  int used = 0;
+  const int p1 = (glob(o1.kind) && used < NSLOT) ? used++ : -1;
+  const int p2 = (glob(o2.kind) && used < NSLOT) ? used++ : -1;
+  const int p3 = (nops > 2 && glob(o3.kind) && used < NSLOT) ? used++ : -1;
+  const int p4 = (nops > 3 && glob(o4.kind) && used < NSLOT) ? used++ : -1;
+  float pf[64];
+  auto prefetch = [&](int k0) {
+    if (p1 >= 0) fetch_op<FMT>(o1, k0, pf + p1 * SLOT);
+    if (p2 >= 0) fetch_op<FMT>(o2, k0, pf + p2 * SLOT);
+    if (p3 >= 0) fetch_op<FMT>(o3, k0, pf + p3 * SLOT);
+    if (p4 >= 0) fetch_op<FMT>(o4, k0, pf + p4 * SLOT);
+  };
+  auto stage_now = [&](const Tile* tt, const auto& op, int slot, int k0) {
+    if (slot >= 0) {
+      store_op<FMT>(tt, op, lo, pf + slot * SLOT);
+    } else {
+      float x[32];
+      fetch_op<FMT>(op, k0, x);
+      store_op<FMT>(tt, op, lo, x);
+    }
+  };
+  prefetch(0);
   for (int s = 0; s < ns; ++s) {
     const int k0 = s * KS;
-    store_op<FMT>(t1, o1, lo, pf.x[0]);
-    store_op<FMT>(t2, o2, lo, pf.x[1]);
-    if (all4) {
-      if (nops > 2) store_op<FMT>(t3, o3, lo, x3p);
-      if (nops > 3) store_op<FMT>(t4, o4, lo, x4p);
-    } else if (nops > 2) {
-      float x3[32], x4[32];
-      fetch_op<FMT>(o3, k0, x3);
-      if (nops > 3) fetch_op<FMT>(o4, k0, x4);
-      store_op<FMT>(t3, o3, lo, x3);
-      if (nops > 3) store_op<FMT>(t4, o4, lo, x4);
-    }
+    stage_now(t1, o1, p1, k0);
+    stage_now(t2, o2, p2, k0);
+    if (nops > 2) stage_now(t3, o3, p3, k0);
+    if (nops > 3) stage_now(t4, o4, p4, k0);
     stage_own<FMT>(t1, o1, lo, k0);
     stage_own<FMT>(t2, o2, lo, k0);
     if (nops > 2) stage_own<FMT>(t3, o3, lo, k0);
@@ -446,12 +449,7 @@ __device__ __forceinline__ void kloop_t(MmaBar& mb, const Tile* t1, const Opnd<S
       mma_commit(mb.bar);
     }
     __syncwarp();
-    if (s + 1 < ns) {
-      fetch_op<FMT>(o1, k0 + KS, pf.x[0]);
-      fetch_op<FMT>(o2, k0 + KS, pf.x[1]);
-      if (all4 && nops > 2) fetch_op<FMT>(o3, k0 + KS, x3p);
-      if (all4 && nops > 3) fetch_op<FMT>(o4, k0 + KS, x4p);
-    }
+    if (s + 1 < ns) prefetch(k0 + KS);
     mbar_wait(mb.bar, mb.phase, mb.status);
     mb.phase ^= 1u;
     tc_fence_after();
