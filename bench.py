@@ -78,18 +78,30 @@ def make_inputs(seed, device, dtype, shape=(B, H, L)):
 # roofline bookkeeping: per chunk-head algorithmic FLOPs / compulsory HBM bytes per kernel
 # (the split of the reference algorithm's GEMM list and compulsory traffic)
 # --------------------------------------------------------------------------------------
-def kernel_work(s_in, nc):
+# Tensor-core cost of one algorithmic FLOP in a precision mode, in bf16-MMA equivalents: "highest"
+# is three tf32 passes (tf32 MMAs run at half the bf16 rate), "bf16x3" three bf16 passes.
+MODE_COST = {"highest": 6.0, "bf16x3": 3.0, "default": 1.0, "tf32": 2.0}
+
+
+def kernel_work(s_in, nc, modes):
+    """Per chunk-head: (algorithmic FLOPs, bf16-equivalent MMA FLOPs in the configured modes,
+    compulsory HBM bytes) of each kernel.  The FLOPs are the reference algorithm's dense GEMM count
+    split over the kernels that perform its parts; B4 (four T^2 D products of bwd_intra) is
+    fixed at "highest" (mega.py:13)."""
     t2d = T * T * D
     td2 = T * D * D
     t3 = T ** 3
     td = T * D
+    dot, sol, b3 = (MODE_COST[modes[k]] for k in ("dot_mode", "solve_dot_mode", "b3_dot_mode"))
+    hi = MODE_COST["highest"]
+    f_fi, f_bi = 2 * 4 * t2d + (2 / 3) * t3, 2 * (10 * t2d + 3 * td2 + 2 * t3)
     return {
-        "fwd_intra": (2 * 4 * t2d + (2 / 3) * t3, 6 * s_in * td),
-        "fwd_scan": (2 * 2 * td2, 8 * D * D / nc),
-        "fwd_out": (2 * (t2d + td2), 4 * td),
-        "bwd_pre": (2 * (t2d + td2), 0),
-        "bwd_scan": (2 * 2 * td2, 8 * D * D / nc),
-        "bwd_intra": (2 * (10 * t2d + 3 * td2 + 2 * t3), td * (12 * s_in + 4)),
+        "fwd_intra": (f_fi, 2 * 4 * t2d * dot + (2 / 3) * t3 * sol, 6 * s_in * td),
+        "fwd_scan": (2 * 2 * td2, 2 * 2 * td2 * dot, 8 * D * D / nc),
+        "fwd_out": (2 * (t2d + td2), 2 * (t2d + td2) * dot, 4 * td),
+        "bwd_pre": (2 * (t2d + td2), 2 * (t2d + td2) * b3, 0),
+        "bwd_scan": (2 * 2 * td2, 2 * 2 * td2 * b3, 8 * D * D / nc),
+        "bwd_intra": (f_bi, 2 * 4 * t2d * hi + (f_bi - 2 * 4 * t2d) * b3, td * (12 * s_in + 4)),
     }
 
 
@@ -374,32 +386,34 @@ def run_ours(args):
 
     if rank == 0:
         hbm, tflops, peak_kind = peaks()
-        work = kernel_work(s_in, L // T)
+        modes = {k: cfg.__dict__[k] for k in ("dot_mode", "solve_dot_mode", "b3_dot_mode")}
+        work = kernel_work(s_in, L // T, modes)
         nch = B * H * (L // T)
-        traffic = ncu_traffic()
+        traffic = ncu_traffic() if dtype == torch.float32 else {}
         kern = {}
         for name, (tot_ms, cnt) in prof.items():
             if cnt == 0:
                 continue
             per = tot_ms / cnt
-            f, by = work[name]
-            t_f = f * nch / (tflops * 1e12)
+            f, f_eff, by = work[name]
+            t_f = f_eff * nch / (tflops * 1e12)
             t_b = by * nch / (hbm * 1e9)
-            kern[name] = {"ms_per_launch": per, "share": tot_ms, "flops": f * nch, "bytes": by * nch,
-                          "t_roof_ms": max(t_f, t_b) * 1e3, "bound": "tensor" if t_f >= t_b else "hbm"}
+            kern[name] = {"ms_per_launch": per, "share": tot_ms, "flops": f * nch, "flops_eff": f_eff * nch,
+                          "bytes": by * nch, "t_roof_ms": max(t_f, t_b) * 1e3,
+                          "bound": "tensor" if t_f >= t_b else "hbm"}
         tot = sum(k["share"] for k in kern.values()) or 1.0
         for k in kern.values():
             k["share"] = k["share"] / tot
         dom = max(kern, key=lambda n: kern[n]["share"])
         kd = kern[dom]
         if kd["bound"] == "tensor":
-            achieved, peak, unit = kd["flops"] / (kd["ms_per_launch"] / 1e3) / 1e12, tflops, "TFLOP/s"
+            # algorithmic TFLOP/s against the mode's effective peak (measured bf16 peak / mode cost)
+            achieved = kd["flops"] / (kd["ms_per_launch"] / 1e3) / 1e12
+            peak, unit = tflops * kd["flops"] / kd["flops_eff"], "TFLOP/s"
         else:
             achieved, peak, unit = kd["bytes"] / (kd["ms_per_launch"] / 1e3) / 1e9, hbm, "GB/s"
-        # whole-step roofline (all kernels): algorithmic time over measured step time
-        f_all = sum(v[0] for v in work.values()) * nch * world
-        b_all = sum(v[1] for v in work.values()) * nch * world
-        t_step_roof = max(f_all / world / (tflops * 1e12), b_all / world / (hbm * 1e9)) * 1e3
+        # whole-step roofline: the kernels' roofline times over the measured step time
+        t_step_roof = sum(k["t_roof_ms"] for k in kern.values())
         cpu = None
         if world == 1:
             val_cpu, cores = cpu_sample_tokens_per_s(3, 1)
@@ -418,6 +432,8 @@ def run_ours(args):
                        "l2": "inputs (6 x 25 MB) and residuals (~250 MB) exceed the 126 MB L2"},
             "roofline": {"kernel": dom, "bound": kd["bound"], "achieved": achieved, "peak": peak, "unit": unit,
                          "frac": achieved / peak, "traffic": traffic.get(dom), "peak_source": peak_kind,
+                         "peak_note": "tensor peak = measured sustained bf16 dense peak / the precision mode's "
+                                      "MMA cost per FLOP (3 x tf32 = 6, 3 x bf16 = 3, bf16 = 1)",
                          "step_frac": t_step_roof / ms},
             "kernels": {n: {"ms": round(v["ms_per_launch"], 4), "share": round(v["share"], 3),
                             "bound": v["bound"], "roof_ms": round(v["t_roof_ms"], 4)} for n, v in kern.items()},
