@@ -226,6 +226,19 @@ def test_wide_gate_spans_match_oracle(g_wide):
     _compare(_run_op(cfg, xs, h0), _run_oracle(cfg, xs, h0), 1e-4)
 
 
+def test_wide_gate_spans_bf16_inputs_and_default_modes():
+    """The wide-channel kernels with bf16 inputs and all-bf16 products (the launches run with
+    runtime modes): o / h_final / dh0 at the bf16-product tolerance, gradients in bf16."""
+    cfg = make_cfg().with_(dot_mode="default", solve_dot_mode="default", b3_dot_mode="default")
+    xs, h0 = O.bench_inputs(1, 1, 256, D, 4, dtype=torch.bfloat16)
+    xs = list(xs)
+    g = xs[5].float()
+    g[..., :32] = -3.0
+    xs[5] = g.to(torch.bfloat16)
+    got, want = _run_op(cfg, xs, h0), _run_oracle(cfg, [x.float() for x in xs], h0)
+    _compare(got, want, 2e-2)
+
+
 def test_positive_gate_raises():
     cfg = make_cfg()
     xs, _ = O.bench_inputs(1, 1, 128, D, 0)
