@@ -10,7 +10,9 @@
 //   bwd_intra  (chunk-parallel)  everything else: dv_new, B3 (WY / inverse gradients), B4 and B5.
 //
 // bwd_intra folds the gate factors into the operands so that the six gradients accumulate in
-// four tensor-memory accumulators.  With m the chunk's per-channel reference point,
+// four tensor-memory accumulators.  B3's dA = dwp' kb^T + dv_new (w v)^T is evaluated as
+// dv_new X^T with X = w v - kb h_pre (kb = b k e^gc), and A^T dwp' as -(A^T dv_new) h_pre^T, which
+// saves one product; the two B4 products with k F share one staging of k F.  With m the chunk's per-channel reference point,
 // E = e^(gc - m), F = e^(m - gc):
 //   Dq  = E o [ do (scale e^m h_pre)^T          + scale dAqk (k F) ]            = dq
 //   Dbk = E o [ A^T dwp'                        + dAkk (k F) ]                  = dL/d(b k)
@@ -315,6 +317,15 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
     for (int j = 0; j < 4; ++j) x[j] = sanitize(x[j] * ex(fminf(gl_s[c0 + j] - gr[j], 0.f)), clip);
   };
   auto src_dhn = [&](int r, int c0, float* x) { ld4_f(dhn_g + r * kD + c0, x); };
+  auto src_h = [&](int r, int c0, float* x) { ld4_f(hpre_g + r * kD + c0, x); };
+  auto src_kb = [&](int r, int c0, float* x) {  // b k e^min(gc, 0)
+    float kv[4];
+    ld4_in(b + r * kD + c0, x);
+    ld4_in(k + r * kD + c0, kv);
+    const float* gr = gcrow(r) + c0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) x[j] = x[j] * kv[j] * ex(fminf(gr[j], 0.f));
+  };
   auto src_hpre_em = [&](int r, int c0, float* x) {  // row d = r of e^m h_pre
     ld4_f(hpre_g + r * kD + c0, x);
     const float s = ex(mid_s[r]);
@@ -326,14 +337,6 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
     const float s = ex(gl_s[r] - mzE_s[r]);
 #pragma unroll
     for (int j = 0; j < 4; ++j) x[j] *= s;
-  };
-  auto src_bkE = [&](int r, int c0, float* x) {
-    float kv[4];
-    ld4_in(b + r * kD + c0, x);
-    ld4_in(k + r * kD + c0, kv);
-    const float* gr = gcrow(r) + c0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) x[j] = x[j] * kv[j] * ex(gr[j] - mid_s[c0 + j]);
   };
   auto src_bkEz = [&](int r, int c0, float* x) {  // b k E, zero in wide channels (B4 operand)
     float kv[4];
@@ -354,13 +357,6 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
     const float* gr = gcrow(r) + c0;
 #pragma unroll
     for (int j = 0; j < 4; ++j) x[j] = x[j] * ex(mzF_s[c0 + j] - gr[j]);
-  };
-  auto src_wv = [&](int r, int c0, float* x) {
-    float vv[4];
-    ld4_in(w + r * kD + c0, x);
-    ld4_in(v + r * kD + c0, vv);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) x[j] *= vv[j];
   };
   auto src_ainv = [&](int r, int c0, float* x) { ld4_f(ainv_g + r * kT + c0, x); };
   auto src_vnew = [&](int r, int c0, float* x) { ld4_f(vnew_g + r * kD + c0, x); };
@@ -397,11 +393,29 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
     }
   }
   sync_all();
-  // 2. S1 = dwp' = -dv_new (e^m h_pre)^T                                          [B3]
-  gemm1(m3, pool, mb, S1, kmaj(tm(S0)), kany(src_hpre_em), true, false);
-  // 3. S2 = dA = sanitize(dwp' (bk E)^T + dv_new (w v)^T)                          [B3]
-  gemm2(m3, pool, mb, S2, kmaj(tm(S1)), kany(src_bkE), false, false, S2, kmaj(tm(S0)), kany(src_wv), false, true,
-        false, false);
+  // 2. S1 = X = w v - kb h_pre  (kb = b k e^gc; X^T is v_new's pre-image under A: v_new = A X)
+  //    [B3].  With dwp' = -dv_new (h_pre)^T (the gate factors cancel), the reference's
+  //    dA = dwp' kb^T + dv_new (w v)^T is dv_new X^T, and A^T dwp' (step 7) is -dwv h_pre^T.
+  gemm1(m3, pool, mb, S1, kany(src_kb), mn_any(src_h), false, false);
+  {
+    float w4[64], v4[64];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      ld16_in(w + t * kD + cb + 16 * j, w4 + 16 * j);
+      ld16_in(v + t * kD + cb + 16 * j, v4 + 16 * j);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float x[16];
+      tmem_ld16(S1, cb + 16 * j, x);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) x[i] = w4[16 * j + i] * v4[16 * j + i] - x[i];
+      tmem_st16(S1, cb + 16 * j, x);
+    }
+  }
+  sync_all();
+  // 3. S2 = dA = sanitize(dv_new X^T)                                                [B3]
+  gemm1(m3, pool, mb, S2, kmaj(tm(S0)), kmaj(tm(S1)), false, false);
   for (int c0 = cb; c0 < cb + 64; c0 += 16) {
     float x[16];
     tmem_ld16(S2, c0, x);
@@ -410,7 +424,7 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
     tmem_st16(S2, c0, x);
   }
   sync_all();
-  // 4. S3 = dwv = A^T dv_new;  dw = dwv v, dv = dwv w                              [B3]
+  // 4. S3 = dwv = A^T dv_new;  dw = dwv v, dv = dwv w  (dwv stays in S3 for step 7) [B3]
   gemm1(m3, pool, mb, S3, mn_any(src_ainv), mn_own(tm(S0)), false, false);
   {
     float* xb = xbuf(sm);
@@ -457,9 +471,6 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
     }
   }
   sync_all();
-  // 7. S0 = A^T dwp' (B3)  +  dAkk (k F) (B4, highest)
-  gemm1(m3, pool, mb, S0, mn_any(src_ainv), mn_own(tm(S1)), false, false);
-  gemm1(mh, pool, mb, S0, kmaj(tm(S2)), mn_any(src_kF), false, true);
   // 8. S1 = dAqk = (do v_new^T) causal                                              [B2]
   gemm1(m3, pool, mb, S1, kany(src_do), kany(src_vnew), false, false);
   for (int c0 = cb; c0 < cb + 64; c0 += 16) {
@@ -470,9 +481,13 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
     tmem_st16(S1, c0, x);
   }
   sync_all();
-  // 9. S3 = scale do (e^m h_pre)^T (B3)  +  scale dAqk (k F) (B4)
+  // 7a. S0 = A^T dwp' = -dwv (e^m h_pre)^T                                          [B3]
+  gemm1(m3, pool, mb, S0, kmaj(tm(S3)), kany(src_hpre_em), true, false);
+  // 9a. S3 = scale do (e^m h_pre)^T                                                 [B3]
   gemm1(m3, pool, mb, S3, kany(src_do_s), kany(src_hpre_em), false, false);
-  gemm1(mh, pool, mb, S3, kmaj(tm_scaled(S1)), mn_any(src_kF), false, true);
+  // 7b + 9b. S0 += dAkk (k F),  S3 += scale dAqk (k F)    (one staging of k F)      [B4, highest]
+  gemm2(mh, pool, mb, S0, kmaj(tm(S2)), mn_any(src_kF), false, true, S3, kmaj(tm_scaled(S1)), mn_any(NoSrc()),
+        false, true, false, true);
   // 10.-11. finish dq and db;  S3 <- dgc partial;  S0 <- Dbk b E (pre-scaled dk partial).
   //     Wide channels (m = 0): their B4 terms were left out of the products above and are added
   //     exactly here, and S0 keeps Dbk b (their dk is finished without the F leg in step 13).
