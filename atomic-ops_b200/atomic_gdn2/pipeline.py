@@ -14,6 +14,9 @@ place of jax.custom_vjp:
   result is bit-identical to one launch sequence per segment, because the scans store and reload
   the carried state unchanged at a boundary and every other kernel is chunk-local.  Residuals
   are the same size either way (the reference also keeps every segment's residuals);
+* the batch is split into GDN2_STREAMS (default 2) contiguous groups whose launch sequences run
+  on separate streams (joined before returning), so one group's low-occupancy scans and
+  last-wave tails overlap the other group's chunk kernels;
 * backward returns gradients for all seven arguments, each in its input's dtype after the final
   sanitize at 1e4 (pipeline.py:11-14, 38-47); do and dh_final are taken as fp32 (pipeline.py:42).
 
@@ -112,6 +115,27 @@ def _fin(x: torch.Tensor, dt: torch.dtype, cfg: BLRConfig) -> torch.Tensor:
                             posinf=_FINAL_CLIP, neginf=-_FINAL_CLIP).to(dt)
 
 
+_nstreams = max(1, int(os.environ.get("GDN2_STREAMS", "2")))
+_side = {}
+
+
+def _streams(dev: torch.device, n: int):
+    """n side streams of a device (created once): batch groups run on them concurrently."""
+    lst = _side.setdefault(dev.index, [])
+    while len(lst) < n:
+        lst.append(torch.cuda.Stream(device=dev))
+    return lst[:n]
+
+
+def _batch_groups(B: int):
+    """Contiguous batch ranges [b0, b1) processed as independent launch sequences.  Their kernels
+    overlap on the GPU: one group's low-occupancy scans and last-wave tails run beside the other
+    group's chunk kernels (the batch entries are independent recurrences)."""
+    n = min(_nstreams, B)
+    step = -(-B // n)
+    return [(b0, min(B, b0 + step)) for b0 in range(0, B, step)]
+
+
 class _GDN2(torch.autograd.Function):
     @staticmethod
     def forward(ctx, cfg, scale, need_res, q, k, v, w, b, g, h0):
@@ -122,6 +146,7 @@ class _GDN2(torch.autograd.Function):
         # o shares the inputs' (b, h) strides: the C ABI addresses every (B,H,L,D) tensor of a call
         # with one stride pair (views of longer sequences are consumed without copies)
         o = torch.empty_strided((B, H, L, D), q.stride(), dtype=torch.float32, device=dev)
+        h_final = torch.empty((B, H, D, D), dtype=torch.float32, device=dev)
         status = torch.zeros(1, dtype=torch.int32, device=dev)
         # strides of size-1 dims are never used to form an address; give them canonical values
         sb, sh = q.stride(0), q.stride(1)
@@ -129,34 +154,46 @@ class _GDN2(torch.autograd.Function):
             sh = max(sh, L * D)
         if B == 1:
             sb = max(sb, H * sh)
-        h = h0
-        segments, residuals = [], []
-        for s, e in _segment_groups(lib, cfg, scale, B, H, D, sb, sh, q.dtype, nc):
-            a = s * cfg.bt
-            desc = _make_desc(cfg, scale, B, H, (e - s) * cfg.bt, D, sb, sh, q.dtype)
-            nbytes = lib.gdn2_residual_bytes(ctypes.byref(desc))
-            if nbytes == 0:
-                _lib.check(_lib.ERR_INVALID_ARGUMENT, "gdn2_residual_bytes")
-            res = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-            h_out = torch.empty((B, H, D, D), dtype=torch.float32, device=dev)
-            off = a * D
-            el = q.element_size()
-            ins = [ctypes.c_void_p(t.data_ptr() + off * el) for t in (q, k, v, w, b, g)]
-            rc = lib.gdn2_fwd(ctypes.byref(desc), *ins, _ptr(h), ctypes.c_void_p(o.data_ptr() + off * 4),
-                              _ptr(h_out), _ptr(res), _ptr(status), _stream())
-            _lib.check(rc, "gdn2_fwd")
-            segments.append(_Segment(desc, s, e))
-            residuals.append(res if need_res else None)
-            h = h_out
+        el = q.element_size()
+        groups = _batch_groups(B)
+        main = torch.cuda.current_stream(dev)
+        streams = _streams(dev, len(groups)) if len(groups) > 1 else [main]
+        plan = []
+        for (b0, b1), st in zip(groups, streams):
+            if st is not main:
+                st.wait_stream(main)
+            Bg = b1 - b0
+            with torch.cuda.stream(st):
+                h = None if h0 is None else h0[b0:b1]
+                segs = []
+                seg_groups = _segment_groups(lib, cfg, scale, Bg, H, D, sb, sh, q.dtype, nc)
+                for si, (s, e) in enumerate(seg_groups):
+                    desc = _make_desc(cfg, scale, Bg, H, (e - s) * cfg.bt, D, sb, sh, q.dtype)
+                    nbytes = lib.gdn2_residual_bytes(ctypes.byref(desc))
+                    if nbytes == 0:
+                        _lib.check(_lib.ERR_INVALID_ARGUMENT, "gdn2_residual_bytes")
+                    res = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+                    last = si == len(seg_groups) - 1
+                    h_out = h_final[b0:b1] if last else torch.empty((Bg, H, D, D), dtype=torch.float32, device=dev)
+                    off = b0 * sb + s * cfg.bt * D
+                    ins = [ctypes.c_void_p(t.data_ptr() + off * el) for t in (q, k, v, w, b, g)]
+                    rc = lib.gdn2_fwd(ctypes.byref(desc), *ins, _ptr(h), ctypes.c_void_p(o.data_ptr() + off * 4),
+                                      _ptr(h_out), _ptr(res), _ptr(status), _stream())
+                    _lib.check(rc, "gdn2_fwd")
+                    segs.append((_Segment(desc, s, e), res if need_res else None))
+                    h = h_out
+            plan.append((b0, b1, segs))
+        for st in streams:
+            if st is not main:
+                main.wait_stream(st)
         global _last_status
         _last_status = status
         if _checks:
             _raise_on_status(status, "gdn2_fwd")
-        ctx.cfg, ctx.segments = cfg, segments
+        ctx.cfg, ctx.plan = cfg, plan
         ctx.h0_dtype = None if h0 is None else h0.dtype
-        ctx.residuals = residuals
         ctx.save_for_backward(q, k, v, w, b, g)
-        return o, h
+        return o, h_final
 
     @staticmethod
     def backward(ctx, do, dhf):
@@ -165,7 +202,7 @@ class _GDN2(torch.autograd.Function):
         q, k, v, w, b, g = ctx.saved_tensors
         B, H, L, D = q.shape
         dev = q.device
-        if any(r is None for r in ctx.residuals):
+        if any(res is None for _, _, segs in ctx.plan for _, res in segs):
             raise RuntimeError("gdn2: backward through a call made without gradient tracking")
         # every (B,H,L,D) tensor of a call shares the inputs' strides (see forward)
         do_s = torch.empty_strided((B, H, L, D), q.stride(), dtype=torch.float32, device=dev)
@@ -173,21 +210,36 @@ class _GDN2(torch.autograd.Function):
             do_s.zero_()
         else:
             do_s.copy_(do)
-        do = do_s
-        dh = None if dhf is None else dhf.to(torch.float32).contiguous()
+        dhf32 = None if dhf is None else dhf.to(torch.float32).contiguous()
         grads = [torch.empty_strided(t.shape, q.stride(), dtype=t.dtype, device=dev) for t in (q, k, v, w, b, g)]
+        dh0_all = torch.empty((B, H, D, D), dtype=torch.float32, device=dev)
         status = torch.zeros(1, dtype=torch.int32, device=dev)
         el = q.element_size()
-        for sgm, res in zip(reversed(ctx.segments), reversed(ctx.residuals)):
-            off = sgm.a * cfg.bt * D
-            ws = torch.empty(lib.gdn2_bwd_workspace_bytes(ctypes.byref(sgm.desc)), dtype=torch.uint8, device=dev)
-            dh0 = torch.empty((B, H, D, D), dtype=torch.float32, device=dev)
-            ins = [ctypes.c_void_p(t.data_ptr() + off * el) for t in (q, k, v, w, b, g)]
-            outs = [ctypes.c_void_p(t.data_ptr() + off * el) for t in grads]
-            rc = lib.gdn2_bwd(ctypes.byref(sgm.desc), *ins, _ptr(res), ctypes.c_void_p(do.data_ptr() + off * 4),
-                              _ptr(dh), *outs, _ptr(dh0), _ptr(ws), _ptr(status), _stream())
-            _lib.check(rc, "gdn2_bwd")
-            dh = dh0
+        sb = ctx.plan[0][2][0][0].desc.stride_b
+        main = torch.cuda.current_stream(dev)
+        streams = _streams(dev, len(ctx.plan)) if len(ctx.plan) > 1 else [main]
+        for (b0, b1, segs), st in zip(ctx.plan, streams):
+            if st is not main:
+                st.wait_stream(main)
+            Bg = b1 - b0
+            with torch.cuda.stream(st):
+                dh = None if dhf32 is None else dhf32[b0:b1]
+                for si, (sgm, res) in enumerate(reversed(segs)):
+                    off = b0 * sb + sgm.a * cfg.bt * D
+                    ws = torch.empty(lib.gdn2_bwd_workspace_bytes(ctypes.byref(sgm.desc)), dtype=torch.uint8,
+                                     device=dev)
+                    first = si == len(segs) - 1
+                    dh0 = dh0_all[b0:b1] if first else torch.empty((Bg, H, D, D), dtype=torch.float32, device=dev)
+                    ins = [ctypes.c_void_p(t.data_ptr() + off * el) for t in (q, k, v, w, b, g)]
+                    outs = [ctypes.c_void_p(t.data_ptr() + off * el) for t in grads]
+                    rc = lib.gdn2_bwd(ctypes.byref(sgm.desc), *ins, _ptr(res),
+                                      ctypes.c_void_p(do_s.data_ptr() + off * 4), _ptr(dh), *outs, _ptr(dh0), _ptr(ws),
+                                      _ptr(status), _stream())
+                    _lib.check(rc, "gdn2_bwd")
+                    dh = dh0
+        for st in streams:
+            if st is not main:
+                main.wait_stream(st)
         global _last_status
         _last_status = status
         if _checks:
@@ -195,7 +247,7 @@ class _GDN2(torch.autograd.Function):
         grads = [_fin(gr, t.dtype, cfg) for gr, t in zip(grads, (q, k, v, w, b, g))]
         dh0 = None
         if ctx.h0_dtype is not None and ctx.needs_input_grad[9]:
-            dh0 = _fin(dh, ctx.h0_dtype, cfg)
+            dh0 = _fin(dh0_all, ctx.h0_dtype, cfg)
         return (None, None, None, *grads, dh0)
 
 
