@@ -70,9 +70,6 @@ def _raise_on_status(st: torch.Tensor, what: str):
     msgs = []
     if code & _lib.DEV_TIMEOUT:
         msgs.append("an on-chip wait timed out (results invalid)")
-    if code & _lib.DEV_SPAN:
-        msgs.append("a chunk's per-channel gate span exceeds the supported range "
-                    "(sum of |g| over one chunk > 128); clamp g (domain.clamp_g) or shorten bt")
     if code & _lib.DEV_POSITIVE_GATE:
         msgs.append("g > 0 seen: outside domain I-1 (g <= 0)")
     raise RuntimeError(f"{what}: " + "; ".join(msgs))

@@ -30,7 +30,6 @@ constexpr int kThreads = 128;  // threads per CTA
 
 // Device status bits (OR-ed into the caller's status word).
 constexpr unsigned kStatusTimeout = 1u;      // an mbarrier wait hit its cycle budget
-constexpr unsigned kStatusSpan = 2u;         // a chunk's gate span exceeds the single-reference range
 constexpr unsigned kStatusPositiveGate = 4u; // g > 0 seen (outside domain I-1)
 
 // ~4 s at 2 GHz: far beyond any legitimate wait in these kernels.

@@ -58,7 +58,7 @@ typedef enum gdn2_dtype { GDN2_F32 = 0, GDN2_BF16 = 1 } gdn2_dtype;
 /* Bits of the device status word the kernels OR into (read it after the stream
  * has been synchronised). */
 #define GDN2_DEV_TIMEOUT 1u        /* a bounded on-chip wait ran out (results invalid) */
-#define GDN2_DEV_SPAN 2u           /* a chunk's per-channel gate span exceeds the supported range */
+#define GDN2_DEV_SPAN 2u           /* reserved: no longer raised (wide gate spans are computed exactly) */
 #define GDN2_DEV_POSITIVE_GATE 4u  /* g > 0 seen: outside domain I-1 (domain.py:1-6) */
 
 /* Operator descriptor.  Fields mirror BLRConfig (config.py:28-50) where they
