@@ -378,17 +378,17 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
   // 1. S0 = dv_new = sanitize(dvl + kg dh_next)                                  [B1, b3 mode]
   gemm1(m3, pool, mb, S0, kany(src_kg), mn_any(src_dhn), false, false);
   {
-    // global loads of the whole half-row first: the TMEM accesses below order all memory
-    // operations, so loads placed between them would each wait out a full latency
-    float y[64];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) ld16_f(dvl_g + t * kD + cb + 16 * j, y + 16 * j);
+    float* xb = xbuf4(sm);
+    xs_fill(xb, 0, dvl_g, kD, cb);
+    xs_fill(xb, 1, dvl_g, kD, cb + 32);
+    xs_wait();
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      float x[16];
+      float x[16], y[16];
+      xs_get16(xb, j >> 1, 16 * (j & 1), y);
       tmem_ld16(S0, cb + 16 * j, x);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) x[i] = sanitize(x[i] + y[16 * j + i], clip);
+      for (int i = 0; i < 16; ++i) x[i] = sanitize(x[i] + y[i], clip);
       tmem_st16(S0, cb + 16 * j, x);
     }
   }
@@ -398,18 +398,20 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
   //    dA = dwp' kb^T + dv_new (w v)^T is dv_new X^T, and A^T dwp' (step 7) is -dwv h_pre^T.
   gemm1(m3, pool, mb, S1, kany(src_kb), mn_any(src_h), false, false);
   {
-    float w4[64], v4[64];
+    float* xb = xbuf4(sm);
+    xs_fill(xb, 0, w, kD, cb);
+    xs_fill(xb, 1, w, kD, cb + 32);
+    xs_fill(xb, 2, v, kD, cb);
+    xs_fill(xb, 3, v, kD, cb + 32);
+    xs_wait();
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      ld16_in(w + t * kD + cb + 16 * j, w4 + 16 * j);
-      ld16_in(v + t * kD + cb + 16 * j, v4 + 16 * j);
-    }
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float x[16];
+      float x[16], w4[16], v4[16];
+      xs_get16(xb, j >> 1, 16 * (j & 1), w4);
+      xs_get16(xb, 2 + (j >> 1), 16 * (j & 1), v4);
       tmem_ld16(S1, cb + 16 * j, x);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) x[i] = w4[16 * j + i] * v4[16 * j + i] - x[i];
+      for (int i = 0; i < 16; ++i) x[i] = w4[i] * v4[i] - x[i];
       tmem_st16(S1, cb + 16 * j, x);
     }
   }
@@ -494,16 +496,21 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
   auto ep1011 = [&](auto wide_tag) {
     constexpr bool kWide = decltype(wide_tag)::value;
     const float* gr = gcrow(t);
-    float* xb = xbuf(sm);
+    float* xb = xbuf4(sm);
 #pragma unroll 1
     for (int hh = 0; hh < 2; ++hh) {
       float q2[32], k2[32], b2[32];
+      xs_fill(xb, 0, q, kD, cb + 32 * hh);
+      xs_fill(xb, 1, k, kD, cb + 32 * hh);
+      xs_fill(xb, 2, b, kD, cb + 32 * hh);
+      xs_wait();
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
-        ld16_in(q + t * kD + cb + 32 * hh + 16 * j, q2 + 16 * j);
-        ld16_in(k + t * kD + cb + 32 * hh + 16 * j, k2 + 16 * j);
-        ld16_in(b + t * kD + cb + 32 * hh + 16 * j, b2 + 16 * j);
+        xs_get16(xb, 0, 16 * j, q2 + 16 * j);
+        xs_get16(xb, 1, 16 * j, k2 + 16 * j);
+        xs_get16(xb, 2, 16 * j, b2 + 16 * j);
       }
+      __syncwarp();  // the blocks are reused for the outputs below
 #pragma unroll
       for (int jj = 0; jj < 2; ++jj) {
         const int c0 = cb + 32 * hh + 16 * jj;
@@ -552,8 +559,15 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
   if constexpr (!WIDE) {
     float* gr = gcs + t * kGcPitch;
     float k4[64];
+    {
+      float* xb = xbuf4(sm);
+      xs_fill(xb, 0, k, kD, cb);
+      xs_fill(xb, 1, k, kD, cb + 32);
+      xs_wait();
 #pragma unroll
-    for (int j = 0; j < 4; ++j) ld16_in(k + t * kD + cb + 16 * j, k4 + 16 * j);
+      for (int j = 0; j < 4; ++j) xs_get16(xb, j >> 1, 16 * (j & 1), k4 + 16 * j);
+      __syncwarp();  // the buffer is reused for dk below
+    }
 #pragma unroll
     for (int jj = 0; jj < 4; ++jj) {
       const int c0 = cb + 16 * jj;
@@ -568,11 +582,11 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
         dgcp[j] -= kv[j] * x[j];
         if (t == kT - 1) dgcp[j] += extra_s[c0 + j] + extra_s[kD + c0 + j];
       }
-      xb_put16(xbuf(sm), c0 - cb, y);
+      xb_put16(xbuf4(sm), c0 - cb, y);
 #pragma unroll
       for (int j = 0; j < 16; ++j) gr[c0 + j] = dgcp[j];
     }
-    xb_flush(xbuf(sm), dk, kD, cb);
+    xb_flush(xbuf4(sm), dk, kD, cb);
   } else {
     // Wide channels: dk[j,d] = (Dbk b)[j,d] + e^(gl-gc[j,d]) (v_new dh_next^T)[j,d]
     //   + sum_{i>=j} (scale dAqk[i,j] q[i,d] + dAkk[i,j] (b k)[i,d]) e^(gc[i,d]-gc[j,d]),
@@ -628,6 +642,7 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
   // 14. dg = reverse cumsum of dgc over the chunk (B5)
   if (tid < kD) {
     float acc = 0.f;
+#pragma unroll 8
     for (int r = kT - 1; r >= 0; --r) {
       acc += gcs[r * kGcPitch + tid];
       const float val = sanitize(acc, clip);

@@ -101,6 +101,11 @@ __device__ __forceinline__ void ld4(const __nv_bfloat16* p, float v[4]) {
   float2 fa = __bfloat1622float2(a), fb = __bfloat1622float2(b);
   v[0] = fa.x; v[1] = fa.y; v[2] = fb.x; v[3] = fb.y;
 }
+// 16-byte asynchronous copy global -> shared (no registers; completion by cp_async_wait_all).
+__device__ __forceinline__ void cp_async16(void* dst_smem, const void* src_gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst_smem)), "l"(src_gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 __device__ __forceinline__ float ld1(const float* p) { return __ldg(p); }
 __device__ __forceinline__ float ld1(const __nv_bfloat16* p) { return __bfloat162float(*p); }
 __device__ __forceinline__ void st4(float* p, const float v[4]) {

@@ -415,9 +415,13 @@ __global__ void __launch_bounds__(kCT, 1) fwd_out_kernel(const OpParams p, float
   // v_new = u - S0 (kept in S0 and written as a residual)
   {
     float uv[64];
+    float* xb = xbuf(sm);  // two 1024-float blocks, then the 32 x 64 output block
+    xs_fill(xb, 0, u_g, kD, cb);
+    xs_fill(xb, 1, u_g, kD, cb + 32);
+    xs_wait();
 #pragma unroll
-    for (int j = 0; j < 4; ++j) ld16_f(u_g + t * kD + cb + 16 * j, uv + 16 * j);
-    float* xb = xbuf(sm);
+    for (int j = 0; j < 4; ++j) xs_get16(xb, j >> 1, 16 * (j & 1), uv + 16 * j);
+    __syncwarp();  // the buffer is reused for v_new below
 #pragma unroll
     for (int jj = 0; jj < 4; ++jj) {
       const int c0 = cb + 16 * jj;

@@ -589,6 +589,52 @@ __device__ __forceinline__ void xb_flush(float* xb, TOut* dst, int ld, int cb) {
   __syncwarp();
 }
 
+// The reverse direction, for epilogues that combine an accumulator row with global operands:
+// global rows 32 (warp & 3) + r, columns c0..c0+31 -> 32 x 32 block `blk` of a warp buffer (each
+// warp-wide access covers four 128-byte row segments; fp32 by asynchronous copies), after which
+// every lane reads its own row with xs_get16 (after xs_wait).  A thread's row read directly from
+// global memory makes each warp-wide access touch 32 rows (32 L1 wavefronts), which made those
+// loads the longest part of the epilogues.  Blocks are 1024 floats, 16-byte chunk j of row r at
+// chunk position j ^ (r & 7): conflict-free for both access patterns.
+__device__ __forceinline__ int xs_off(int r, int chunk) { return r * 32 + ((chunk ^ (r & 7)) << 2); }
+__device__ __forceinline__ void xs_fill(float* xb, int blk, const float* src, int ld, int c0) {
+  const int r0 = ((threadIdx.x >> 5) & 3) * 32, lane = threadIdx.x & 31;
+  float* b = xb + blk * 1024;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int lr = 4 * i + (lane >> 3), ck = lane & 7;
+    cp_async16(b + xs_off(lr, ck), src + (size_t)(r0 + lr) * ld + c0 + 4 * ck);
+  }
+}
+__device__ __forceinline__ void xs_fill(float* xb, int blk, const __nv_bfloat16* src, int ld, int c0) {
+  const int r0 = ((threadIdx.x >> 5) & 3) * 32, lane = threadIdx.x & 31;
+  float* b = xb + blk * 1024;
+  float v[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ld4(src + (size_t)(r0 + 4 * i + (lane >> 3)) * ld + c0 + 4 * (lane & 7), v[i]);
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    *reinterpret_cast<float4*>(b + xs_off(4 * i + (lane >> 3), lane & 7)) = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
+}
+__device__ __forceinline__ void xs_wait() {
+  cp_async_wait_all();
+  __syncwarp();
+}
+// This thread's row (its lane), 16 columns at local column c (0 or 16) of block `blk`.
+__device__ __forceinline__ void xs_get16(const float* xb, int blk, int c, float* x) {
+  const int r = threadIdx.x & 31;
+  const float* b = xb + blk * 1024;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float4 v = *reinterpret_cast<const float4*>(b + xs_off(r, (c >> 2) + i));
+    x[4 * i] = v.x; x[4 * i + 1] = v.y; x[4 * i + 2] = v.z; x[4 * i + 3] = v.w;
+  }
+}
+// A warp buffer of four such blocks: warp w's region starts at w * 4096 floats of the operand pool.
+__device__ __forceinline__ float* xbuf4(uint8_t* pool_base) {
+  return reinterpret_cast<float*>(pool_base) + (threadIdx.x >> 5) * 4096;
+}
+
 // Row loaders (16 values)
 template <class TIn>
 __device__ __forceinline__ void ld16_in(const TIn* p, float* x) {
