@@ -254,6 +254,28 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
     mbar_init(bar, 1);
     fence_mbar_init();
   }
+  // L2 prefetch hints, about two products ahead of each chunk tile's first use (the kernel is
+  // latency-bound; an L2 hit shortens the first K-slice of every product)
+  constexpr uint32_t kInTile = kT * kD * sizeof(TIn), kF32Tile = kT * kD * 4;
+  auto l2_ahead = [&](int stage) {
+    if (tid != 0) return;
+    if (stage == 0) {
+      l2_prefetch(k, kInTile);
+      l2_prefetch(dvl_g, kF32Tile);
+      l2_prefetch(b, kInTile);
+      l2_prefetch(hpre_g, kF32Tile);
+    } else if (stage == 1) {
+      l2_prefetch(w, kInTile);
+      l2_prefetch(v, kInTile);
+      l2_prefetch(ainv_g, kF32Tile);
+    } else if (stage == 2) {
+      l2_prefetch(do_, kF32Tile);
+      l2_prefetch(vnew_g, kF32Tile);
+    } else {
+      l2_prefetch(q, kInTile);
+    }
+  };
+  l2_ahead(0);
   {
     float mx, mn;
     bool pos;
@@ -375,6 +397,7 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
     };
   };
 
+  l2_ahead(1);
   // 1. S0 = dv_new = sanitize(dvl + kg dh_next)                                  [B1, b3 mode]
   gemm1(m3, pool, mb, S0, kany(src_kg), mn_any(src_dhn), false, false);
   {
@@ -416,6 +439,7 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
     }
   }
   sync_all();
+  l2_ahead(2);
   // 3. S2 = dA = sanitize(dv_new X^T)                                                [B3]
   gemm1(m3, pool, mb, S2, kmaj(tm(S0)), kmaj(tm(S1)), false, false);
   for (int c0 = cb; c0 < cb + 64; c0 += 16) {
@@ -460,6 +484,7 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
     tmem_st16(S0, c0, x);
   }
   sync_all();
+  l2_ahead(3);
   // 6. S2 = dAkk = sanitize(-(1-eps) A^T tmp) strict                                  [B3]
   gemm1(m3, pool, mb, S2, mn_any(src_ainv), mn_own(tm(S0)), true, false);
   {
