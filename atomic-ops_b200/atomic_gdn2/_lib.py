@@ -37,7 +37,8 @@ class Gdn2Desc(ctypes.Structure):
 
 EXPORTS = ("gdn2_residual_bytes", "gdn2_bwd_workspace_bytes", "gdn2_fwd", "gdn2_bwd",
            "gdn2_status_string", "gdn2_selftest_gemm", "gdn2_profile_enable", "gdn2_profile_collect",
-           "gdn2_fwd_noalloc", "gdn2_prologue_fwd", "gdn2_prologue_bwd", "gdn2_selftest_engine")
+           "gdn2_fwd_noalloc", "gdn2_prologue_fwd", "gdn2_prologue_bwd", "gdn2_selftest_engine",
+           "gdn2_selftest_wait_timeout")
 # kernel ids of gdn2_profile_collect
 KERNELS = ("fwd_intra", "fwd_scan", "fwd_out", "bwd_pre", "bwd_scan", "bwd_intra")
 
@@ -64,6 +65,8 @@ def _declare(lib):
     lib.gdn2_fwd_noalloc.argtypes = [ctypes.POINTER(Gdn2Desc)] + [P] * 11
     lib.gdn2_selftest_engine.restype = ctypes.c_int
     lib.gdn2_selftest_engine.argtypes = [P] * 5 + [ctypes.c_int32] * 3 + [P, P]
+    lib.gdn2_selftest_wait_timeout.restype = ctypes.c_int
+    lib.gdn2_selftest_wait_timeout.argtypes = [P, ctypes.c_int64, P, P]
     I64 = ctypes.c_int64
     lib.gdn2_prologue_fwd.restype = ctypes.c_int
     lib.gdn2_prologue_fwd.argtypes = [P, I64, I64, I64, I64, ctypes.c_float, ctypes.c_int32] + [P] * 7

@@ -233,7 +233,32 @@ static cudaError_t launch_engine_b(int bk, const float* A, const float* At, cons
   return launch_engine<AK, 2>(A, At, B, Bt, C, prec, st, s);
 }
 
+// Failure-detection self-test: one warp waits on an mbarrier phase that nothing completes, with
+// the same bounded wait every kernel of the library uses, so the wait must run out, set the
+// timeout bit and return; the elapsed cycles are reported.  No fault, trap or endless loop.
+__global__ void selftest_wait_kernel(unsigned* st, long long limit, long long* cycles) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  const long long t0 = clock64();
+  const bool done = mbar_wait_for(&bar, 0u, st, limit);
+  const long long dt = clock64() - t0;
+  if (threadIdx.x == 0) *cycles = done ? -1 : dt;
+}
+
 }  // namespace gdn2
+
+extern "C" gdn2_status gdn2_selftest_wait_timeout(uint32_t* dev_status, int64_t limit_cycles, int64_t* dev_cycles,
+                                                  void* stream) {
+  using namespace gdn2;
+  if (!dev_status || !dev_cycles || limit_cycles <= 0 || limit_cycles > kWaitCycles) return GDN2_ERR_INVALID_ARGUMENT;
+  selftest_wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(dev_status, (long long)limit_cycles,
+                                                            reinterpret_cast<long long*>(dev_cycles));
+  return cudaGetLastError() == cudaSuccess ? GDN2_OK : GDN2_ERR_CUDA;
+}
 
 extern "C" gdn2_status gdn2_selftest_engine(const float* A, const float* At, const float* B, const float* Bt, float* C,
                                             int32_t precision, int32_t a_kind, int32_t b_kind, uint32_t* dev_status,

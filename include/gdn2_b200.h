@@ -134,6 +134,17 @@ gdn2_status gdn2_selftest_engine(const float* A, const float* At, const float* B
                                  int32_t precision, int32_t a_kind, int32_t b_kind, uint32_t* dev_status,
                                  void* stream);
 
+/*
+ * Failure-detection self-test (no reference counterpart; the reference's device code has no
+ * waits): one warp waits, with the bounded on-chip wait every kernel of the library uses, on a
+ * barrier phase that nothing completes.  The wait gives up after limit_cycles SM cycles
+ * (0 < limit_cycles <= the library's own bound of 8e9), ORs GDN2_DEV_TIMEOUT into *dev_status
+ * and stores the cycles it waited in *dev_cycles (-1 if the phase had completed).  Shows that a
+ * stuck wait ends as a status bit the host reads while the context stays usable.
+ */
+gdn2_status gdn2_selftest_wait_timeout(uint32_t* dev_status, int64_t limit_cycles, int64_t* dev_cycles,
+                                       void* stream);
+
 /* Allocation-free forward (no counterpart in the reference).  Same arguments and results as
  * gdn2_fwd minus the residual buffer: the scratch lives in a fixed 64 MiB device array inside the
  * library, so the call performs no device allocation.  It is meant for callers that cannot

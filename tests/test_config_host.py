@@ -99,6 +99,12 @@ def test_entry_points_reject_bad_arguments_without_gpu():
     assert rc == _lib.ERR_INVALID_ARGUMENT
     rc = lib.gdn2_bwd(ctypes.byref(_desc()), *[null] * 19)
     assert rc == _lib.ERR_INVALID_ARGUMENT
+    # the wait self-test refuses a missing status word and limits outside (0, 8e9] cycles
+    rc = lib.gdn2_selftest_wait_timeout(null, 1000, null, null)
+    assert rc == _lib.ERR_INVALID_ARGUMENT
+    one = ctypes.c_void_p(16)  # never dereferenced: the limit check fails first
+    for bad in (0, -5, 8 * 10 ** 9 + 1):
+        assert lib.gdn2_selftest_wait_timeout(one, bad, one, null) == _lib.ERR_INVALID_ARGUMENT
     assert _lib.status_string(0) == "ok" and "invalid" in _lib.status_string(1)
     with pytest.raises(ValueError):
         _lib.check(_lib.ERR_INVALID_ARGUMENT, "x")

@@ -260,3 +260,31 @@ def test_strided_views_without_copy():
         o1, h1 = make_blr_trainable(cfg, 0.1)(*views, h0.to(dev))
         o2, h2 = make_blr_trainable(cfg, 0.1)(*(v.contiguous() for v in views), h0.to(dev))
     assert torch.equal(o1, o2) and torch.equal(h1, h2)
+
+
+def test_stuck_wait_ends_as_status_and_context_survives():
+    """Failure detection without a GPU fault: a bounded on-chip wait on a barrier phase that nothing
+    completes (the wait every kernel uses, with a ~0.05 s limit) must give up, set the timeout bit
+    of the status word, and leave the context usable for the next operator call."""
+    import ctypes
+    from atomic_gdn2 import _lib
+    lib = _lib.load()
+    dev = torch.device("cuda:0")
+    st = torch.zeros(1, dtype=torch.int32, device=dev)
+    cyc = torch.zeros(1, dtype=torch.int64, device=dev)
+    limit = 100_000_000
+    rc = lib.gdn2_selftest_wait_timeout(ctypes.c_void_p(st.data_ptr()), limit, ctypes.c_void_p(cyc.data_ptr()),
+                                        ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert int(st.item()) & _lib.DEV_TIMEOUT
+    assert limit <= int(cyc.item()) < 4 * limit
+    # the host turns the bit into an error on the operator path, and the next call runs cleanly
+    with pytest.raises(RuntimeError, match="timed out"):
+        atomic_gdn2.pipeline._raise_on_status(st, "gdn2")
+    cfg = make_cfg()
+    xs, h0 = O.bench_inputs(1, 1, 256, D, 3)
+    got = _run_op(cfg, xs, h0)
+    want = _run_oracle(cfg, xs, h0)
+    _compare(got, want, 1e-4)
+    assert atomic_gdn2.last_status() == 0
