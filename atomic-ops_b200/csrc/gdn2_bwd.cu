@@ -147,15 +147,16 @@ __global__ void __launch_bounds__(kCT, 1) bwd_pre_kernel(const BwdParams P) {
 // c0..c0+15 (zero for channels that are not wide).  dAqk / dAkk rows come from TMEM (this
 // thread's lane); every thread of the warp runs the same loads.
 template <class TIn>
-__device__ __forceinline__ void wide_dq_dbk(uint32_t S1, uint32_t S2, const TIn* __restrict__ k, const float* gcs,
-                                            const float* wide_s, int i, int c0, float scale, float* oq, float* ob) {
+__device__ __forceinline__ void wide_dq_dbk(uint32_t aqk_slot, uint32_t akk_slot, const TIn* __restrict__ k,
+                                            const float* gcs, const float* wide_s, int i, int c0, float scale,
+                                            float* oq, float* ob) {
 #pragma unroll
   for (int j = 0; j < 16; ++j) oq[j] = ob[j] = 0.f;
 #pragma unroll 1
   for (int jc = 0; jc < kT; jc += 16) {
     float aq[16], ak[16];
-    tmem_ld16(S1, (uint32_t)jc, aq);
-    tmem_ld16(S2, (uint32_t)jc, ak);
+    tmem_ld16(aqk_slot, (uint32_t)jc, aq);
+    tmem_ld16(akk_slot, (uint32_t)jc, ak);
 #pragma unroll 1
     for (int dd = 0; dd < 16; ++dd) {
       const int d = c0 + dd;
@@ -498,24 +499,24 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
     }
   }
   sync_all();
-  // 8. S1 = dAqk = (do v_new^T) causal                                              [B2]
-  gemm1(m3, pool, mb, S1, kany(src_do), kany(src_vnew), false, false);
+  // 7a + 9a (one staging of e^m h_pre):  S0 = A^T dwp' = -dwv (e^m h_pre)^T,
+  //     S1 = scale do (e^m h_pre)^T  (the Dq accumulator from here on)                 [B3]
+  gemm2(m3, pool, mb, S0, kmaj(tm(S3)), kany(src_hpre_em), true, false, S1, kany(src_do_s), kany(NoSrc()), false,
+        false, false, true);
+  // 8. S3 = dAqk = (do v_new^T) causal  (dwv, read by 7a, is no longer needed)       [B2]
+  gemm1(m3, pool, mb, S3, kany(src_do), kany(src_vnew), false, false);
   for (int c0 = cb; c0 < cb + 64; c0 += 16) {
     float x[16];
-    tmem_ld16(S1, c0, x);
+    tmem_ld16(S3, c0, x);
 #pragma unroll
     for (int j = 0; j < 16; ++j) x[j] = (c0 + j <= t) ? x[j] : 0.f;
-    tmem_st16(S1, c0, x);
+    tmem_st16(S3, c0, x);
   }
   sync_all();
-  // 7a. S0 = A^T dwp' = -dwv (e^m h_pre)^T                                          [B3]
-  gemm1(m3, pool, mb, S0, kmaj(tm(S3)), kany(src_hpre_em), true, false);
-  // 9a. S3 = scale do (e^m h_pre)^T                                                 [B3]
-  gemm1(m3, pool, mb, S3, kany(src_do_s), kany(src_hpre_em), false, false);
-  // 7b + 9b. S0 += dAkk (k F),  S3 += scale dAqk (k F)    (one staging of k F)      [B4, highest]
-  gemm2(mh, pool, mb, S0, kmaj(tm(S2)), mn_any(src_kF), false, true, S3, kmaj(tm_scaled(S1)), mn_any(NoSrc()),
+  // 7b + 9b. S0 += dAkk (k F),  S1 += scale dAqk (k F)    (one staging of k F)      [B4, highest]
+  gemm2(mh, pool, mb, S0, kmaj(tm(S2)), mn_any(src_kF), false, true, S1, kmaj(tm_scaled(S3)), mn_any(NoSrc()),
         false, true, false, true);
-  // 10.-11. finish dq and db;  S3 <- dgc partial;  S0 <- Dbk b E (pre-scaled dk partial).
+  // 10.-11. finish dq and db;  S1 <- dgc partial;  S0 <- Dbk b E (pre-scaled dk partial).
   //     Wide channels (m = 0): their B4 terms were left out of the products above and are added
   //     exactly here, and S0 keeps Dbk b (their dk is finished without the F leg in step 13).
   auto ep1011 = [&](auto wide_tag) {
@@ -543,10 +544,10 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
         const float* kv = k2 + 16 * jj;
         const float* bv = b2 + 16 * jj;
         float x[16], y[16], E[16], dgcp[16], wq[16], wb[16];
-        if constexpr (kWide) wide_dq_dbk(S1, S2, k, gcs, wide_s, t, c0, scale, wq, wb);
+        if constexpr (kWide) wide_dq_dbk(S3, S2, k, gcs, wide_s, t, c0, scale, wq, wb);
 #pragma unroll
         for (int j = 0; j < 16; ++j) E[j] = ex(gr[c0 + j] - mid_s[c0 + j]);
-        tmem_ld16(S3, c0, x);  // Dq / E
+        tmem_ld16(S1, c0, x);  // Dq / E
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           x[j] *= E[j];
@@ -566,7 +567,7 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
           else x[j] = x[j] * bv[j] * E[j];
         }
         xb2_put16(xb, 1, 16 * jj, y);
-        tmem_st16(S3, c0, dgcp);
+        tmem_st16(S1, c0, dgcp);
         tmem_st16(S0, c0, x);
       }
       xb2_flush(xb, 0, dq, kD, cb + 32 * hh);
@@ -577,9 +578,9 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
   sync_all();
   // 12. S0 += v_new (e^(gl-m) dh_next)^T (B3)  +  scale dAqk^T (q E) + dAkk^T (bk E) (B4)
   gemm1(m3, pool, mb, S0, kany(src_vnew), kany(src_dhn_gl), false, true);
-  gemm2(mh, pool, mb, S0, mn_own(tm(S1)), mn_any(src_qE), false, true, S0, mn_own(tm(S2)), mn_any(src_bkEz), false,
+  gemm2(mh, pool, mb, S0, mn_own(tm(S3)), mn_any(src_qE), false, true, S0, mn_own(tm(S2)), mn_any(src_bkEz), false,
         true, false, false);
-  // 13. dk = F o S0;  dgc = S3 - k o dk (+ decay term on the last row).  dgc overwrites this
+  // 13. dk = F o S0;  dgc = S1 - k o dk (+ decay term on the last row).  dgc overwrites this
   //     thread's own half-row of gcs (no other thread reads that row any more).
   if constexpr (!WIDE) {
     float* gr = gcs + t * kGcPitch;
@@ -599,7 +600,7 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
       const float* kv = k4 + 16 * jj;
       float x[16], y[16], dgcp[16];
       tmem_ld16(S0, c0, x);
-      tmem_ld16(S3, c0, dgcp);
+      tmem_ld16(S1, c0, dgcp);
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         x[j] *= ex(mid_s[c0 + j] - gr[c0 + j]);
@@ -621,7 +622,7 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
 #pragma unroll 1
     for (int c0 = cb; c0 < cb + 64; c0 += 16) {
       float a1[16], a2[16];
-      tmem_ld16(S1, c0, a1);
+      tmem_ld16(S3, c0, a1);
       tmem_ld16(S2, c0, a2);
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
@@ -639,7 +640,7 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
       float x[16], y[16], dgcp[16], kv[16];
       ld16_in(k + t * kD + c0, kv);
       tmem_ld16(S0, c0, x);
-      tmem_ld16(S3, c0, dgcp);
+      tmem_ld16(S1, c0, dgcp);
 #pragma unroll 1
       for (int j = 0; j < 16; ++j) {
         const int d = c0 + j;
