@@ -441,8 +441,10 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
   }
   sync_all();
   l2_ahead(2);
-  // 3. S2 = dA = sanitize(dv_new X^T)                                                [B3]
-  gemm1(m3, pool, mb, S2, kmaj(tm(S0)), kmaj(tm(S1)), false, false);
+  // 3. + 4. in one K-loop (independent products):  S2 = dA = sanitize(dv_new X^T),
+  //     S3 = dwv = A^T dv_new;  dw = dwv v, dv = dwv w  (dwv stays in S3 for step 7) [B3]
+  gemm2(m3, pool, mb, S2, kmaj(tm(S0)), kmaj(tm(S1)), false, false, S3, mn_any(src_ainv), mn_own(tm(S0)), false,
+        false, false, false);
   for (int c0 = cb; c0 < cb + 64; c0 += 16) {
     float x[16];
     tmem_ld16(S2, c0, x);
@@ -450,9 +452,6 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
     for (int j = 0; j < 16; ++j) x[j] = sanitize(x[j], clip);
     tmem_st16(S2, c0, x);
   }
-  sync_all();
-  // 4. S3 = dwv = A^T dv_new;  dw = dwv v, dv = dwv w  (dwv stays in S3 for step 7) [B3]
-  gemm1(m3, pool, mb, S3, mn_any(src_ainv), mn_own(tm(S0)), false, false);
   {
     float* xb = xbuf(sm);
     tmem_to_xbuf(S3, cb, xb);
@@ -473,7 +472,7 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
       st4(dw + (r0 + lr) * kD + c0, y);
       st4(dv + (r0 + lr) * kD + c0, z);
     }
-    __syncthreads();  // the buffers live in the operand pool the next product stages into
+    sync_all();  // the buffers live in the operand pool the next product stages into
   }
   // 5. S0 = tmp = sanitize(dA A^T)                                                   [B3]
   gemm1(m3, pool, mb, S0, kmaj(tm(S2)), kany(src_ainv), false, false);
