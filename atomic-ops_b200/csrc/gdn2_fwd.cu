@@ -25,8 +25,9 @@
 // WY inverse.  With N = I + Se (Se = (1-eps) Akk, strictly lower), Dg its four 32x32 diagonal
 // blocks and R the strictly block-lower rest, N^-1 = (I - W)(I + W^2) Dg^-1 with W = Dg^-1 R
 // (W^4 = 0).  Dg^-1 comes from warp-level forward substitution (one warp per block, lane =
-// column, fp32); the four remaining products run on the tensor core in solve_dot_mode.  This
-// replaces the reference's leaf + block-doubling ladder (fwd/solve.py:9-43).
+// column, fp32); the four remaining products run on the tensor core in solve_dot_mode, as three
+// dependent K-loops: W, then W^2 and W Dg^-1 together, then W^2 Q with Q = (I - W) Dg^-1, so that
+// N^-1 = Q + W^2 Q.  This replaces the reference's leaf + block-doubling ladder (fwd/solve.py:9-43).
 #include <type_traits>
 
 #include "gdn2_kernels.cuh"
@@ -270,30 +271,31 @@ __global__ void __launch_bounds__(kCT, 1) fwd_intra_kernel(const OpParams p) {
   }
   __syncthreads();
 
-  // ---- 4.-7. A = (I - W)(I + W^2) Dg^-1,  W = Dg^-1 R                          (solve mode) --------
+  // ---- 4.-7. A = (I + W^2)(I - W) Dg^-1 = Q + W^2 Q,  Q = Dg^-1 - W Dg^-1,  W = Dg^-1 R   (solve mode)
+  //      three dependent K-loops: W; then W^2 and W Dg^-1 sharing the staged W; then W^2 Q
   gemm1(ms, pool, mbar, S0, kmaj(src_dinv), mn_own(src_R), false, false);   // W -> S0
-  gemm1(ms, pool, mbar, S2, kmaj(tm(S0)), mn_own(tm(S0)), false, false);    // W^2 -> S2
-  gemm1(ms, pool, mbar, S3, kmaj(tm(S2)), mn_any(src_dinv4), false, false);  // W^2 Dg^-1 -> S3
-  for (int c0 = cb; c0 < cb + 64; c0 += 16) {                               // P = S3 + Dg^-1
+  gemm2(ms, pool, mbar, S2, kmaj(tm(S0)), mn_own(tm(S0)), false, false, S3, kmaj(NoSrc()), mn_any(src_dinv4), false,
+        false, true, false);                                                 // W^2 -> S2, W Dg^-1 -> S3
+  for (int c0 = cb; c0 < cb + 64; c0 += 16) {                               // Q = Dg^-1 - W Dg^-1 -> S3
     float x[16], dv[16];
     tmem_ld16(S3, c0, x);
     src_dinv(t, c0, dv);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) x[j] += dv[j];
+    for (int j = 0; j < 16; ++j) x[j] = dv[j] - x[j];
     tmem_st16(S3, c0, x);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  gemm1(ms, pool, mbar, S2, kmaj(tm(S0)), mn_own(tm(S3)), false, false);    // W P -> S2
+  gemm1(ms, pool, mbar, S0, kmaj(tm(S2)), mn_own(tm(S3)), false, false);    // W^2 Q -> S0
   {
     float* xb = xbuf(sm);
-    for (int c0 = cb; c0 < cb + 64; c0 += 16) {                             // A = sanitize(P - W P)
+    for (int c0 = cb; c0 < cb + 64; c0 += 16) {                             // A = sanitize(Q + W^2 Q)
       float x[16], y[16];
       tmem_ld16(S3, c0, x);
-      tmem_ld16(S2, c0, y);
+      tmem_ld16(S0, c0, y);
 #pragma unroll
-      for (int j = 0; j < 16; ++j) x[j] = (c0 + j <= t) ? sanitize(x[j] - y[j], clip) : 0.f;
+      for (int j = 0; j < 16; ++j) x[j] = (c0 + j <= t) ? sanitize(x[j] + y[j], clip) : 0.f;
       tmem_st16(S1, c0, x);
       xb_put16(xb, c0 - cb, x);
     }
