@@ -67,7 +67,7 @@ __global__ void __launch_bounds__(kCT, 1) bwd_pre_kernel(const BwdParams P) {
   const float clip = p.clip, scale = p.scale;
 
   if (warp == 0) {
-    tmem_alloc(tslot, 256);
+    tmem_alloc(tslot, 512);  // three accumulators (allocations are powers of two)
     tmem_relinquish();
   }
   if (tid == 0) {
@@ -83,7 +83,7 @@ __global__ void __launch_bounds__(kCT, 1) bwd_pre_kernel(const BwdParams P) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tb = *tslot;
-  const uint32_t S0 = tb, S1 = tb + 128;
+  const uint32_t S0 = tb, S1 = tb + 128, S2 = tb + 256;
   MmaBar mb{bar, 0u, p.status};
 
   // global row sources: 4 values of row r from column c0 (mn_any operands)
@@ -114,21 +114,20 @@ __global__ void __launch_bounds__(kCT, 1) bwd_pre_kernel(const BwdParams P) {
     xb_flush(xb, dvl_g, kD, cb);
   }
   __syncthreads();  // the buffers live in the operand pool the next product stages into
-  // S1 -= wp^T dvl
-  gemm1(m3, pool, mb, S1, mn_any(src_wp), mn_own(tm0), true, true);
+  // S1 -= wp^T dvl  and  S2 = wp^T kg  (one staging of wp^T): Cc, and the transposed transition
+  // of this chunk for the reverse scan, M^T = diag(e^gl) - wp^T kg
+  gemm2(m3, pool, mb, S1, mn_any(src_wp), mn_own(tm0), true, true, S2, mn_any(NoSrc()), mn_any(src_kg), false, false,
+        true, false);
   {
     float* xb = xbuf(sm);
     tmem_to_xbuf(S1, cb, xb);
     xb_flush(xb, cc_g, kD, cb);
   }
-  __syncthreads();
-  // transposed transition of this chunk for the reverse scan: M^T = diag(e^gl) - wp^T kg
-  gemm1(m3, pool, mb, S0, mn_any(src_wp), mn_any(src_kg), false, false);
   {
     const float dec = ex(fminf(gcs[(kT - 1) * kGcPitch + t], 0.f));
     for (int c0 = cb; c0 < cb + 64; c0 += 16) {
       float x[16];
-      tmem_ld16(S0, c0, x);
+      tmem_ld16(S2, c0, x);
 #pragma unroll
       for (int j = 0; j < 16; ++j) x[j] = ((c0 + j) == t ? dec : 0.f) - x[j];
       image_store8(mb_g, m3, t, c0, x);
@@ -137,7 +136,7 @@ __global__ void __launch_bounds__(kCT, 1) bwd_pre_kernel(const BwdParams P) {
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tb, 256);
+  if (warp == 0) tmem_dealloc(tb, 512);
 }
 
 // ---------------------------------------------------------------------------------------
