@@ -398,28 +398,13 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
   };
 
   l2_ahead(1);
-  // 1. S0 = dv_new = sanitize(dvl + kg dh_next)                                  [B1, b3 mode]
-  gemm1(m3, pool, mb, S0, kany(src_kg), mn_any(src_dhn), false, false);
-  {
-    float* xb = xbuf4(sm);
-    xs_fill(xb, 0, dvl_g, kD, cb);
-    xs_fill(xb, 1, dvl_g, kD, cb + 32);
-    xs_wait();
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float x[16], y[16];
-      xs_get16(xb, j >> 1, 16 * (j & 1), y);
-      tmem_ld16(S0, cb + 16 * j, x);
-#pragma unroll
-      for (int i = 0; i < 16; ++i) x[i] = sanitize(x[i] + y[i], clip);
-      tmem_st16(S0, cb + 16 * j, x);
-    }
-  }
-  sync_all();
-  // 2. S1 = X = w v - kb h_pre  (kb = b k e^gc; X^T is v_new's pre-image under A: v_new = A X)
-  //    [B3].  With dwp' = -dv_new (h_pre)^T (the gate factors cancel), the reference's
-  //    dA = dwp' kb^T + dv_new (w v)^T is dv_new X^T, and A^T dwp' (step 7) is -dwv h_pre^T.
-  gemm1(m3, pool, mb, S1, kany(src_kb), mn_any(src_h), false, false);
+  // 1. + 2. in one K-loop (independent products)                                    [B1, B3]
+  //  1. S0 = dv_new = sanitize(dvl + kg dh_next)
+  //  2. S1 = X = w v - kb h_pre  (kb = b k e^gc; X^T is v_new's pre-image under A: v_new = A X).
+  //     With dwp' = -dv_new (h_pre)^T (the gate factors cancel), the reference's
+  //     dA = dwp' kb^T + dv_new (w v)^T is dv_new X^T, and A^T dwp' (step 7) is -dwv h_pre^T.
+  gemm2(m3, pool, mb, S0, kany(src_kg), mn_any(src_dhn), false, false, S1, kany(src_kb), mn_any(src_h), false, false,
+        false, false);
   {
     float* xb = xbuf4(sm);
     xs_fill(xb, 0, w, kD, cb);
@@ -436,6 +421,19 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
 #pragma unroll
       for (int i = 0; i < 16; ++i) x[i] = w4[i] * v4[i] - x[i];
       tmem_st16(S1, cb + 16 * j, x);
+    }
+    __syncwarp();  // the warp's blocks are refilled below
+    xs_fill(xb, 0, dvl_g, kD, cb);
+    xs_fill(xb, 1, dvl_g, kD, cb + 32);
+    xs_wait();
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float x[16], y[16];
+      xs_get16(xb, j >> 1, 16 * (j & 1), y);
+      tmem_ld16(S0, cb + 16 * j, x);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) x[i] = sanitize(x[i] + y[i], clip);
+      tmem_st16(S0, cb + 16 * j, x);
     }
   }
   sync_all();
