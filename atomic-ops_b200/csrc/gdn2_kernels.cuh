@@ -195,15 +195,24 @@ __device__ __forceinline__ int crow() { return threadIdx.x & 127; }
 __device__ __forceinline__ int chalf() { return threadIdx.x >> 7; }
 
 // Column-wise inclusive cumsum of the chunk's gate g (T x D) into shared memory
-// gcs[t * kGcPitch + d].  The chunk is loaded cooperatively with coalesced 16-byte loads (all
-// threads, many loads in flight), then thread d < 128 scans channel d in shared memory and
-// returns the channel's max, min and whether a positive gate was seen.
+// gcs[t * kGcPitch + d].  The chunk is copied cooperatively (coalesced 16-byte copies, all
+// threads, all in flight), then thread d < 128 scans channel d in shared memory and returns the
+// channel's max, min and whether a positive gate was seen.
 // (pipeline.py:21 / ref.py:14: gc = cumsum(g) per chunk.)
 constexpr int kGcPitch = 132;  // padded row pitch (floats): conflict-free row reads by row owners
 
-template <class TIn>
-__device__ __forceinline__ void chunk_cumsum(const TIn* __restrict__ g, float* gcs, float& mx, float& mn,
-                                             bool& pos) {
+// The chunk's gate tile g (kT x kD) -> gcs (row pitch kGcPitch): fp32 by asynchronous copies
+// (complete at chunk_cumsum_finish; the caller may issue other loads meanwhile), bf16 through
+// registers.
+__device__ __forceinline__ void chunk_gate_issue(const float* __restrict__ g, float* gcs) {
+  const int tid = threadIdx.x;
+#pragma unroll
+  for (int i = tid; i < kT * (kD / 4); i += kCT) {
+    const int r = i >> 5, c4 = (i & 31) * 4;
+    cp_async16(gcs + r * kGcPitch + c4, g + r * kD + c4);
+  }
+}
+__device__ __forceinline__ void chunk_gate_issue(const __nv_bfloat16* __restrict__ g, float* gcs) {
   const int tid = threadIdx.x;
 #pragma unroll 8
   for (int i = tid; i < kT * (kD / 4); i += kCT) {
@@ -212,6 +221,12 @@ __device__ __forceinline__ void chunk_cumsum(const TIn* __restrict__ g, float* g
     ld4(g + r * kD + c4, v);
     *reinterpret_cast<float4*>(gcs + r * kGcPitch + c4) = make_float4(v[0], v[1], v[2], v[3]);
   }
+}
+// In-place cumulative sum of gcs over the chunk's rows (one thread per channel), with the
+// per-channel max / min of the cumsum and whether any gate is positive.
+__device__ __forceinline__ void chunk_cumsum_finish(float* gcs, float& mx, float& mn, bool& pos) {
+  const int tid = threadIdx.x;
+  cp_async_wait_all();
   __syncthreads();
   mx = -3.0e38f;
   mn = 3.0e38f;
@@ -228,6 +243,12 @@ __device__ __forceinline__ void chunk_cumsum(const TIn* __restrict__ g, float* g
       mn = fminf(mn, acc);
     }
   }
+}
+template <class TIn>
+__device__ __forceinline__ void chunk_cumsum(const TIn* __restrict__ g, float* gcs, float& mx, float& mn,
+                                             bool& pos) {
+  chunk_gate_issue(g, gcs);
+  chunk_cumsum_finish(gcs, mx, mn, pos);
 }
 
 // ---------------------------------------------------------------------------
