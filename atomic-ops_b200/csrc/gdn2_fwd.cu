@@ -318,7 +318,6 @@ __global__ void __launch_bounds__(kCT, 1) fwd_intra_kernel(const OpParams p) {
         tmem_ld16(slot, c0, x);
 #pragma unroll
         for (int j = 0; j < 16; ++j) x[j] = sanitize(x[j], clip);
-        tmem_st16(slot, c0, x);
         xb_put16(xb, c0 - cb, x);
       }
       xb_flush(xb, pass ? u_g : wp_g, kD, cb);
@@ -329,7 +328,12 @@ __global__ void __launch_bounds__(kCT, 1) fwd_intra_kernel(const OpParams p) {
   tc_fence_after();
 
   // ---- 9. M = diag(e^gl) - kg^T wp -> S1,  Bc = kg^T u -> S3                  (dot mode) --------
-  gemm2(md, pool, mbar, S1, mn_any(src_kg), mn_own(tm(S0)), false, false, S3, mn_any(NoSrc()), mn_own(tm(S2)),
+  //      wp and u are read back from the residual tiles just written (L2) rather than staged from
+  //      TMEM: a TMEM-backed MN-major operand can only be staged by the two warps owning the slice's
+  //      lanes, a global one by all eight
+  auto src_wp_res = [&](int r, int c0, float* x) { ld4_cg(wp_g + r * kD + c0, x); };
+  auto src_u_res = [&](int r, int c0, float* x) { ld4_cg(u_g + r * kD + c0, x); };
+  gemm2(md, pool, mbar, S1, mn_any(src_kg), mn_any(src_wp_res), false, false, S3, mn_any(NoSrc()), mn_any(src_u_res),
         false, false, true, false);
   {
     const float dec = ex(fminf(gl_s[t], 0.f));

@@ -532,6 +532,11 @@ __device__ __forceinline__ void gemm2(Mode m, uint32_t pool, MmaBar& mb, uint32_
 // 4-value row loaders of the coalesced (kany / mn_any) sources
 template <class TIn>
 __device__ __forceinline__ void ld4_in(const TIn* p, float* x) { ld4(p, x); }
+// 4 fp32 values written earlier by this kernel (L2, bypassing the incoherent read-only path)
+__device__ __forceinline__ void ld4_cg(const float* p, float* x) {
+  const float4 v = __ldcg(reinterpret_cast<const float4*>(p));
+  x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+}
 __device__ __forceinline__ void ld4_f(const float* p, float* x) {
   const float4 v = *reinterpret_cast<const float4*>(p);
   x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
