@@ -103,7 +103,6 @@ __global__ void __launch_bounds__(kCT, 1) bwd_pre_kernel(const BwdParams P) {
     for (int j = 0; j < 4; ++j) x[j] = sanitize(x[j] * ex(fminf(gl[j] - gr[j], 0.f)), clip);
   };
   auto src_wp = [&](int r, int c0, float* x) { ld4_f(wp_g + r * kD + c0, x); };
-  auto tm0 = [&](int, int c0, float* x) { tmem_ld16(S0, (uint32_t)c0, x); };
 
   // S0 = Aqk^T do, S1 = (scale qg)^T do   (shared B = do)
   gemm2(m3, pool, mb, S0, mn_any(src_aqk), mn_any(src_do), false, false, S1, mn_any(src_qg), mn_any(NoSrc()), false,
@@ -115,9 +114,11 @@ __global__ void __launch_bounds__(kCT, 1) bwd_pre_kernel(const BwdParams P) {
   }
   __syncthreads();  // the buffers live in the operand pool the next product stages into
   // S1 -= wp^T dvl  and  S2 = wp^T kg  (one staging of wp^T): Cc, and the transposed transition
-  // of this chunk for the reverse scan, M^T = diag(e^gl) - wp^T kg
-  gemm2(m3, pool, mb, S1, mn_any(src_wp), mn_own(tm0), true, true, S2, mn_any(NoSrc()), mn_any(src_kg), false, false,
-        true, false);
+  // of this chunk for the reverse scan, M^T = diag(e^gl) - wp^T kg.  dvl is read back from the tile
+  // just written (L2), so that all warps stage it (from TMEM only the lane owners could)
+  auto src_dvl_res = [&](int r, int c0, float* x) { ld4_cg(dvl_g + r * kD + c0, x); };
+  gemm2(m3, pool, mb, S1, mn_any(src_wp), mn_any(src_dvl_res), true, true, S2, mn_any(NoSrc()), mn_any(src_kg), false,
+        false, true, false);
   {
     float* xb = xbuf(sm);
     tmem_to_xbuf(S1, cb, xb);
@@ -242,6 +243,8 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
   const float* vnew_g = reinterpret_cast<const float*>(p.res + p.rl.vnew) + (size_t)ch * mat;
   const float* dvl_g = reinterpret_cast<const float*>(P.ws + P.wl.dvl) + (size_t)ch * mat;
   const float* dhn_g = reinterpret_cast<const float*>(P.ws + P.wl.dhs) + (size_t)ch * mat;
+  float* daqk_g = reinterpret_cast<float*>(P.ws + P.wl.daqk) + (size_t)ch * mat;
+  float* dakk_g = reinterpret_cast<float*>(P.ws + P.wl.dakk) + (size_t)ch * mat;
   const Mode m3 = mode_from_enum(B3 >= 0 ? B3 : p.b3_mode);
   const Mode mh = mode_from_enum(GDN2_PREC_HIGHEST);  // B4 products are fixed at "highest" (mega.py:13)
   const float clip = p.clip, scale = p.scale;
@@ -486,13 +489,16 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
   gemm1(m3, pool, mb, S2, mn_any(src_ainv), mn_own(tm(S0)), true, false);
   {
     const float keep = 1.0f - p.eps;
+    float* xb = xbuf(sm);
     for (int c0 = cb; c0 < cb + 64; c0 += 16) {
       float x[16];
       tmem_ld16(S2, c0, x);
 #pragma unroll
       for (int j = 0; j < 16; ++j) x[j] = (c0 + j < t) ? sanitize(x[j] * keep, clip) : 0.f;
       tmem_st16(S2, c0, x);
+      xb_put16(xb, c0 - cb, x);
     }
+    xb_flush(xb, dakk_g, kT, cb);  // read back by step 12 (all warps stage it from there)
   }
   sync_all();
   // 7a + 9a (one staging of e^m h_pre):  S0 = A^T dwp' = -dwv (e^m h_pre)^T,
@@ -501,12 +507,17 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
         false, false, true);
   // 8. S3 = dAqk = (do v_new^T) causal  (dwv, read by 7a, is no longer needed)       [B2]
   gemm1(m3, pool, mb, S3, kany(src_do), kany(src_vnew), false, false);
-  for (int c0 = cb; c0 < cb + 64; c0 += 16) {
-    float x[16];
-    tmem_ld16(S3, c0, x);
+  {
+    float* xb = xbuf(sm);
+    for (int c0 = cb; c0 < cb + 64; c0 += 16) {
+      float x[16];
+      tmem_ld16(S3, c0, x);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) x[j] = (c0 + j <= t) ? x[j] : 0.f;
-    tmem_st16(S3, c0, x);
+      for (int j = 0; j < 16; ++j) x[j] = (c0 + j <= t) ? x[j] : 0.f;
+      tmem_st16(S3, c0, x);
+      xb_put16(xb, c0 - cb, x);
+    }
+    xb_flush(xb, daqk_g, kT, cb);  // read back by step 12
   }
   sync_all();
   // 7b + 9b. S0 += dAkk (k F),  S1 += scale dAqk (k F)    (one staging of k F)      [B4, highest]
@@ -574,7 +585,11 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
   sync_all();
   // 12. S0 += v_new (e^(gl-m) dh_next)^T (B3)  +  scale dAqk^T (q E) + dAkk^T (bk E) (B4)
   gemm1(m3, pool, mb, S0, kany(src_vnew), kany(src_dhn_gl), false, true);
-  gemm2(mh, pool, mb, S0, mn_own(tm(S3)), mn_any(src_qE), false, true, S0, mn_own(tm(S2)), mn_any(src_bkEz), false,
+  //     dAqk^T and dAkk^T come back from the tiles steps 8 and 6 wrote (L2): all warps stage them, where
+  //     from TMEM only the two warps owning a slice's lanes could
+  auto src_daqk_res = [&](int r, int c0, float* x) { ld4_cg(daqk_g + r * kT + c0, x); };
+  auto src_dakk_res = [&](int r, int c0, float* x) { ld4_cg(dakk_g + r * kT + c0, x); };
+  gemm2(mh, pool, mb, S0, mn_any(src_daqk_res), mn_any(src_qE), false, true, S0, mn_any(src_dakk_res), mn_any(src_bkEz), false,
         true, false, false);
   // 13. dk = F o S0;  dgc = S1 - k o dk (+ decay term on the last row).  dgc overwrites this
   //     thread's own half-row of gcs (no other thread reads that row any more).

@@ -413,7 +413,6 @@ __global__ void __launch_bounds__(kCT, 1) fwd_out_kernel(const OpParams p, float
   };
   auto src_h = [&](int r, int c0, float* x) { ld4_f(h_g + r * kD + c0, x); };
   auto src_aqk = [&](int r, int c0, float* x) { ld4_f(aqk_g + r * kT + c0, x); };
-  auto tm0 = [&](int, int c0, float* x) { tmem_ld16(S0, (uint32_t)c0, x); };
 
   // S0 = wp h_pre,  S1 = (scale qg) h_pre   (shared B = h_pre)
   gemm2(md, pool, mbar, S0, kany(src_wp), mn_any(src_h), false, false, S1, kany(src_qg), mn_any(NoSrc()), false,
@@ -436,15 +435,16 @@ __global__ void __launch_bounds__(kCT, 1) fwd_out_kernel(const OpParams p, float
 #pragma unroll
       for (int j = 0; j < 16; ++j) x[j] = uv[16 * jj + j] - x[j];
       xb_put16(xb, c0 - cb, x);
-      tmem_st16(S0, c0, x);
     }
     xb_flush(xb, vn_g, kD, cb);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  // S1 += Aqk v_new
-  gemm1(md, pool, mbar, S1, kany(src_aqk), mn_own(tm0), false, true);
+  // S1 += Aqk v_new, v_new read back from the residual tile just written (L2): all warps stage it,
+  // where a TMEM-backed MN-major operand is staged by the two warps owning each slice's lanes
+  auto src_vn_res = [&](int r, int c0, float* x) { ld4_cg(vn_g + r * kD + c0, x); };
+  gemm1(md, pool, mbar, S1, kany(src_aqk), mn_any(src_vn_res), false, true);
   {
     float* xb = xbuf(sm);
     for (int c0 = cb; c0 < cb + 64; c0 += 16) {

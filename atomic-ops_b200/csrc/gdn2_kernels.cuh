@@ -44,7 +44,7 @@ __host__ __device__ inline ResLayout res_layout(int BH, int NC, Mode fwd_scan) {
 
 // Backward workspace layout.
 struct WsLayout {
-  size_t dvl, cc, dhs, mb, total;
+  size_t dvl, cc, dhs, daqk, dakk, mb, total;
   uint32_t mb_stride;  // bytes per chunk-head of the backward (transposed) transition image
 };
 __host__ __device__ inline WsLayout ws_layout(int BH, int NC, Mode bwd_scan) {
@@ -57,6 +57,8 @@ __host__ __device__ inline WsLayout ws_layout(int BH, int NC, Mode bwd_scan) {
   w.dvl = o; o = align256(o + nch * mat);
   w.cc = o; o = align256(o + nch * mat);
   w.dhs = o; o = align256(o + nch * mat);  // dh entering each chunk from the right
+  w.daqk = o; o = align256(o + nch * mat);  // bwd_intra's dAqk and dAkk, read back by its last product
+  w.dakk = o; o = align256(o + nch * mat);
   w.total = o;
   return w;
 }

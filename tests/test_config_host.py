@@ -76,8 +76,8 @@ def test_residual_sizes_and_validation():
     lib = _lib.load()
     ok = lib.gdn2_residual_bytes(ctypes.byref(_desc()))
     assert ok > 0 and ok % 256 == 0
-    # dvl, Cc, dh states (fp32) + the transposed transition image (bf16x3: 64 KB per chunk-head)
-    assert lib.gdn2_bwd_workspace_bytes(ctypes.byref(_desc())) == 3 * 2 * 2 * 128 * 128 * 4 + 2 * 2 * 65536
+    # dvl, Cc, dh states, dAqk, dAkk (fp32) + the transposed transition image (bf16x3: 64 KB per chunk-head)
+    assert lib.gdn2_bwd_workspace_bytes(ctypes.byref(_desc())) == 5 * 2 * 2 * 128 * 128 * 4 + 2 * 2 * 65536
     # fp32 residual scales with the number of chunk-heads
     big = lib.gdn2_residual_bytes(ctypes.byref(_desc(B=4, H=6, L=2048)))
     assert 180e6 < big < 300e6
