@@ -664,12 +664,18 @@ def run_lm(args):
         return float(t.item())
 
     ms = max_over_ranks(ms)
-    # operator kernels inside one step
+    # operator kernels inside one step, with each operator call's batch as one launch sequence so
+    # that launches do not overlap and their durations add up (the timed steps overlap two batch
+    # groups on two streams)
+    import atomic_gdn2.pipeline as _pipe
+    nstreams = _pipe._nstreams
+    _pipe._nstreams = 1
     _lib.profile_enable(True)
     step(batches[0])
     torch.cuda.synchronize()
     prof = _lib.profile_collect()
     _lib.profile_enable(False)
+    _pipe._nstreams = nstreams
     # end to end: tokens from pinned host memory every step, loss read back every step
     host = [b.cpu().pin_memory() for b in batches]
     torch.cuda.synchronize()
@@ -706,7 +712,7 @@ def run_lm(args):
                        {k: cfg.__dict__[k] for k in ("dot_mode", "solve_dot_mode", "b3_dot_mode")},
                        "l2": "activations (~10 GB per step) exceed the 126 MB L2"},
             "operator_kernels_ms_per_step": op_ms,
-            "operator_share": sum(op_ms.values()) / ms,
+            "operator_share": sum(op_ms.values()) / ms,  # of the timed (overlapped) step: an upper bound
             "e2e": {"value": e2e_ms, "unit": "ms", "h2d_bytes_per_step": LM_B * LM_L * 8, "d2h_bytes_per_step": 4},
             "gpu_launches": (op_launches(LM_B, LM_L, cfg) + 2) * len(model.layers) * steps,
             "final_loss": final_loss,
