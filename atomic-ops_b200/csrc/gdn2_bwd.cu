@@ -278,11 +278,11 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
       l2_prefetch(q, kInTile);
     }
   };
-  l2_ahead(0);
   {
     float mx, mn;
     bool pos;
     chunk_cumsum(g, gcs, mx, mn, pos);
+    l2_ahead(0);  // after the gate tile has landed: the hints would compete with its copies
     const bool wide = tid < kD && mx - mn > kSpanMax;
     if (tid < kD) {
       const float mid = 0.5f * (mx + mn);
