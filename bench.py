@@ -137,7 +137,7 @@ def ncu_traffic():
 
 
 # --------------------------------------------------------------------------------------
-# clocks during the timed region
+# host CPUs local to the GPU (placement of the end-to-end pinned buffers)
 # --------------------------------------------------------------------------------------
 def gpu_local_cpus(dev):
     """The host CPUs NVML reports as closest to this GPU (its NUMA node), or None.  Pinned host
@@ -160,6 +160,9 @@ def gpu_local_cpus(dev):
         return None
 
 
+# --------------------------------------------------------------------------------------
+# clocks during the timed region
+# --------------------------------------------------------------------------------------
 class Clocks:
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
