@@ -71,10 +71,13 @@ __device__ __forceinline__ void wide_scores(const TIn* __restrict__ q, const TIn
   }
 }
 
-// WIDE = false: the fast kernel; it records in the residual whether the chunk has wide channels
-// and leaves such chunks to the WIDE = true launch that follows it (which skips all others).
+// WIDE = false: the common path; it records in the residual whether the chunk has wide channels
+// and hands such chunks to the WIDE = true path (an out-of-line call in the same launch).
+template <class TIn>
+__device__ __noinline__ void fwd_intra_wide(const OpParams& p, const int ch);
+
 template <class TIn, int DOT, int SOLVE, bool WIDE>
-__global__ void __launch_bounds__(kCT, 1) fwd_intra_kernel(const OpParams p) {
+__device__ __forceinline__ void fwd_intra_chunk(const OpParams& p, const int ch) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
   const uint32_t pool = smem_u32(sm);
@@ -90,7 +93,7 @@ __global__ void __launch_bounds__(kCT, 1) fwd_intra_kernel(const OpParams p) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t = crow(), half = chalf();
   const int cb = half * 64;  // this thread's 64 columns of its row
-  const int ch = blockIdx.x, bh = ch / p.NC, c = ch % p.NC;
+  const int bh = ch / p.NC, c = ch % p.NC;
   const long long off = chunk_off(p, bh, c);
   const TIn* q = reinterpret_cast<const TIn*>(p.q) + off;
   const TIn* k = reinterpret_cast<const TIn*>(p.k) + off;
@@ -129,7 +132,11 @@ __global__ void __launch_bounds__(kCT, 1) fwd_intra_kernel(const OpParams p) {
     const int any_wide = __syncthreads_or(tid < kD && mx - mn > kSpanMax);
     if constexpr (!WIDE) {
       if (tid == 0) *wide_flag = any_wide;
-      if (any_wide) return;
+      if (any_wide) {
+        __syncthreads();  // the flag is visible to the whole CTA
+        fwd_intra_wide<TIn>(p, ch);
+        return;
+      }
     }
   }
   if (warp == 0) {
@@ -355,6 +362,18 @@ __global__ void __launch_bounds__(kCT, 1) fwd_intra_kernel(const OpParams p) {
   if (warp == 0) tmem_dealloc(tb, 512);
 }
 
+// A chunk with wide channels, out of line: its exact CUDA-core terms need registers that the
+// common path cannot spare, and its rare call costs the common path no launch of its own.
+template <class TIn>
+__device__ __noinline__ void fwd_intra_wide(const OpParams& p, const int ch) {
+  fwd_intra_chunk<TIn, -1, -1, true>(p, ch);
+}
+
+template <class TIn, int DOT, int SOLVE>
+__global__ void __launch_bounds__(kCT, 1) fwd_intra_kernel(const OpParams p) {
+  fwd_intra_chunk<TIn, DOT, SOLVE, false>(p, blockIdx.x);
+}
+
 // ---------------------------------------------------------------------------------------
 // fwd_out: v_new = u - wp h_pre;  o = sanitize(scale qg h_pre + Aqk v_new)
 // ---------------------------------------------------------------------------------------
@@ -466,12 +485,12 @@ __global__ void __launch_bounds__(kCT, 1) fwd_out_kernel(const OpParams p, float
 // ---------------------------------------------------------------------------------------
 // Kernels are compiled with compile-time precision modes for the configurations that matter
 // (the reference's defaults and the all-bf16 mode), and with runtime modes for the rest (-1).
-template <class TIn, int DOT, int SOLVE, bool WIDE>
+template <class TIn, int DOT, int SOLVE>
 static cudaError_t launch_fwd_intra_t(const OpParams& p, int nblocks, cudaStream_t st) {
   static unsigned long long done = 0;
-  cudaError_t e = smem_attr_once(fwd_intra_kernel<TIn, DOT, SOLVE, WIDE>, (int)kIntraSmem, done);
+  cudaError_t e = smem_attr_once(fwd_intra_kernel<TIn, DOT, SOLVE>, (int)kIntraSmem, done);
   if (e != cudaSuccess) return e;
-  fwd_intra_kernel<TIn, DOT, SOLVE, WIDE><<<nblocks, kCT, kIntraSmem, st>>>(p);
+  fwd_intra_kernel<TIn, DOT, SOLVE><<<nblocks, kCT, kIntraSmem, st>>>(p);
   return cudaGetLastError();
 }
 template <class TIn, int DOT>
@@ -482,19 +501,14 @@ static cudaError_t launch_fwd_out_t(const OpParams& p, float* o, int nblocks, cu
   fwd_out_kernel<TIn, DOT><<<nblocks, kCT, kOutSmem, st>>>(p, o);
   return cudaGetLastError();
 }
-// The fast launch, then the launch for chunks with wide channels (runtime modes; it returns at
-// once in every other chunk).
+// One launch; chunks with wide channels take the out-of-line path (runtime modes) inside it.
 template <class TIn>
 static cudaError_t launch_fwd_intra_m(const OpParams& p, int nblocks, cudaStream_t st) {
-  cudaError_t e;
   if (p.dot_mode == GDN2_PREC_HIGHEST && p.solve_mode == GDN2_PREC_BF16X3)
-    e = launch_fwd_intra_t<TIn, GDN2_PREC_HIGHEST, GDN2_PREC_BF16X3, false>(p, nblocks, st);
-  else if (p.dot_mode == GDN2_PREC_DEFAULT && p.solve_mode == GDN2_PREC_DEFAULT)
-    e = launch_fwd_intra_t<TIn, GDN2_PREC_DEFAULT, GDN2_PREC_DEFAULT, false>(p, nblocks, st);
-  else
-    e = launch_fwd_intra_t<TIn, -1, -1, false>(p, nblocks, st);
-  if (e != cudaSuccess) return e;
-  return launch_fwd_intra_t<TIn, -1, -1, true>(p, nblocks, st);
+    return launch_fwd_intra_t<TIn, GDN2_PREC_HIGHEST, GDN2_PREC_BF16X3>(p, nblocks, st);
+  if (p.dot_mode == GDN2_PREC_DEFAULT && p.solve_mode == GDN2_PREC_DEFAULT)
+    return launch_fwd_intra_t<TIn, GDN2_PREC_DEFAULT, GDN2_PREC_DEFAULT>(p, nblocks, st);
+  return launch_fwd_intra_t<TIn, -1, -1>(p, nblocks, st);
 }
 template <class TIn>
 static cudaError_t launch_fwd_out_m(const OpParams& p, float* o, int nblocks, cudaStream_t st) {

@@ -43,10 +43,10 @@ CFG_KW = dict(bt=128, bc=64, score_bs=128, bs2=64, mb=8, wy_eps=0.0,
 
 def op_launches(nb, nl, cfg):
     """This library's kernel launches in one fwd+bwd operator call: per batch group (one launch
-    sequence per stream) and sequence segment, fwd_intra + its wide-channel launch, the forward
-    scan, fwd_out, bwd_pre, the backward scan, bwd_intra + its wide-channel launch."""
+    sequence per stream) and sequence segment, fwd_intra (wide chunks included), the forward scan,
+    fwd_out, bwd_pre, the backward scan, bwd_intra and its wide-channel launch."""
     import atomic_gdn2.pipeline as _pipe
-    return 8 * len(_pipe._batch_groups(nb)) * math.ceil((nl // T) / cfg.max_chunks_per_call)
+    return 7 * len(_pipe._batch_groups(nb)) * math.ceil((nl // T) / cfg.max_chunks_per_call)
 
 
 def parse():
