@@ -107,6 +107,10 @@ __global__ void __launch_bounds__(kCT, 1) bwd_pre_kernel(const BwdParams P) {
   // S0 = Aqk^T do, S1 = (scale qg)^T do   (shared B = do)
   gemm2(m3, pool, mb, S0, mn_any(src_aqk), mn_any(src_do), false, false, S1, mn_any(src_qg), mn_any(NoSrc()), false,
         false, false, true);
+  if (threadIdx.x == 0) {  // L2 hints for the wp^T products below
+    l2_prefetch(wp_g, kT * kD * 4);
+    l2_prefetch(k, kT * kD * sizeof(TIn));
+  }
   {
     float* xb = xbuf(sm);
     tmem_to_xbuf(S0, cb, xb);

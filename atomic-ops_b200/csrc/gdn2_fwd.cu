@@ -257,6 +257,11 @@ __device__ __forceinline__ void fwd_intra_chunk(const OpParams& p, const int ch)
     xb_flush(xb, aqk_g, kT, cb);
   };
   ep2(std::integral_constant<bool, WIDE>{});
+  if (tid == 0) {  // L2 hints for step 8's w and v, first read after the on-chip solve below
+    constexpr uint32_t kInTile = kT * kD * sizeof(TIn);
+    l2_prefetch(w, kInTile);
+    l2_prefetch(v, kInTile);
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -436,6 +441,7 @@ __global__ void __launch_bounds__(kCT, 1) fwd_out_kernel(const OpParams p, float
   // S0 = wp h_pre,  S1 = (scale qg) h_pre   (shared B = h_pre)
   gemm2(md, pool, mbar, S0, kany(src_wp), mn_any(src_h), false, false, S1, kany(src_qg), mn_any(NoSrc()), false,
         false, false, true);
+  if (threadIdx.x == 0) l2_prefetch(aqk_g, kT * kT * 4);  // L2 hint for the Aqk v_new product below
   // v_new = u - S0 (kept in S0 and written as a residual)
   {
     float uv[64];
