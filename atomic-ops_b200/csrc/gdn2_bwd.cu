@@ -41,6 +41,7 @@ __device__ __forceinline__ uint8_t* align1024b(uint8_t* p) {
 // ---------------------------------------------------------------------------------------
 template <class TIn, int B3>
 __global__ void __launch_bounds__(kCT, 1) bwd_pre_kernel(const BwdParams P) {
+  pdl_enter();
   extern __shared__ uint8_t smem_raw[];
   const OpParams& p = P.op;
   uint8_t* sm = align1024b(smem_raw);
@@ -208,6 +209,7 @@ __device__ __forceinline__ float wide_dk(const float* dqT, const float* dkT, con
 // the forward's fwd_intra); each launch returns at once in the other kind of chunk.
 template <class TIn, int B3, bool WIDE>
 __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
+  pdl_enter();
   extern __shared__ uint8_t smem_raw[];
   const OpParams& p = P.op;
   uint8_t* sm = align1024b(smem_raw);
@@ -704,7 +706,8 @@ static cudaError_t launch_bwd_pre_t(const BwdParams& p, int nblocks, cudaStream_
   static unsigned long long done = 0;
   cudaError_t e = smem_attr_once(bwd_pre_kernel<TIn, B3>, (int)kPreSmem, done);
   if (e != cudaSuccess) return e;
-  bwd_pre_kernel<TIn, B3><<<nblocks, kCT, kPreSmem, st>>>(p);
+  e = launch_pdl(bwd_pre_kernel<TIn, B3>, nblocks, kCT, kPreSmem, st, p);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 template <class TIn, int B3, bool WIDE>
@@ -712,7 +715,8 @@ static cudaError_t launch_bwd_intra_t(const BwdParams& p, int nblocks, cudaStrea
   static unsigned long long done = 0;
   cudaError_t e = smem_attr_once(bwd_intra_kernel<TIn, B3, WIDE>, (int)kBwdSmem, done);
   if (e != cudaSuccess) return e;
-  bwd_intra_kernel<TIn, B3, WIDE><<<nblocks, kCT, kBwdSmem, st>>>(p);
+  e = launch_pdl(bwd_intra_kernel<TIn, B3, WIDE>, nblocks, kCT, kBwdSmem, st, p);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 // Compile-time precision for the reference's default B3 mode (bf16x3) and the all-bf16 mode.

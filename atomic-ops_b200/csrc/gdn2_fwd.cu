@@ -376,6 +376,7 @@ __device__ __noinline__ void fwd_intra_wide(const OpParams& p, const int ch) {
 
 template <class TIn, int DOT, int SOLVE>
 __global__ void __launch_bounds__(kCT, 1) fwd_intra_kernel(const OpParams p) {
+  pdl_enter();
   fwd_intra_chunk<TIn, DOT, SOLVE, false>(p, blockIdx.x);
 }
 
@@ -384,6 +385,7 @@ __global__ void __launch_bounds__(kCT, 1) fwd_intra_kernel(const OpParams p) {
 // ---------------------------------------------------------------------------------------
 template <class TIn, int DOT>
 __global__ void __launch_bounds__(kCT, 1) fwd_out_kernel(const OpParams p, float* __restrict__ o_out) {
+  pdl_enter();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
   const uint32_t pool = smem_u32(sm);
@@ -496,7 +498,8 @@ static cudaError_t launch_fwd_intra_t(const OpParams& p, int nblocks, cudaStream
   static unsigned long long done = 0;
   cudaError_t e = smem_attr_once(fwd_intra_kernel<TIn, DOT, SOLVE>, (int)kIntraSmem, done);
   if (e != cudaSuccess) return e;
-  fwd_intra_kernel<TIn, DOT, SOLVE><<<nblocks, kCT, kIntraSmem, st>>>(p);
+  e = launch_pdl(fwd_intra_kernel<TIn, DOT, SOLVE>, nblocks, kCT, kIntraSmem, st, p);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 template <class TIn, int DOT>
@@ -504,7 +507,8 @@ static cudaError_t launch_fwd_out_t(const OpParams& p, float* o, int nblocks, cu
   static unsigned long long done = 0;
   cudaError_t e = smem_attr_once(fwd_out_kernel<TIn, DOT>, (int)kOutSmem, done);
   if (e != cudaSuccess) return e;
-  fwd_out_kernel<TIn, DOT><<<nblocks, kCT, kOutSmem, st>>>(p, o);
+  e = launch_pdl(fwd_out_kernel<TIn, DOT>, nblocks, kCT, kOutSmem, st, p, o);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 // One launch; chunks with wide channels take the out-of-line path (runtime modes) inside it.

@@ -20,6 +20,7 @@ constexpr uint32_t kScanSmem = 1024 + kScanImg + kScanB + 64;
 
 
 __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanParams sp) {
+  pdl_enter();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* img_s = sm;
@@ -142,7 +143,8 @@ cudaError_t launch_scan(const ScanParams& sp, int BH, cudaStream_t st) {
   static unsigned long long done = 0;
   cudaError_t e = smem_attr_once(scan_kernel, (int)kScanSmem, done);
   if (e != cudaSuccess) return e;
-  scan_kernel<<<BH * (kD / kDV), kThreads, kScanSmem, st>>>(sp);
+  e = launch_pdl(scan_kernel, (unsigned)(BH * (kD / kDV)), kThreads, kScanSmem, st, sp);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
