@@ -14,7 +14,7 @@ place of jax.custom_vjp:
   result is bit-identical to one launch sequence per segment, because the scans store and reload
   the carried state unchanged at a boundary and every other kernel is chunk-local.  Residuals
   are the same size either way (the reference also keeps every segment's residuals);
-* the batch is split into GDN2_STREAMS (default 2) contiguous groups whose launch sequences run
+* the batch is split into GDN2_STREAMS (default 4) contiguous groups whose launch sequences run
   on separate streams (joined before returning), so one group's low-occupancy scans and
   last-wave tails overlap the other group's chunk kernels;
 * backward returns gradients for all seven arguments, each in its input's dtype after the final
@@ -112,7 +112,7 @@ def _fin(x: torch.Tensor, dt: torch.dtype, cfg: BLRConfig) -> torch.Tensor:
                             posinf=_FINAL_CLIP, neginf=-_FINAL_CLIP).to(dt)
 
 
-_nstreams = max(1, int(os.environ.get("GDN2_STREAMS", "2")))
+_nstreams = max(1, int(os.environ.get("GDN2_STREAMS", "4")))
 _side = {}
 
 

@@ -668,8 +668,8 @@ def run_lm(args):
 
     ms = max_over_ranks(ms)
     # operator kernels inside one step, with each operator call's batch as one launch sequence so
-    # that launches do not overlap and their durations add up (the timed steps overlap two batch
-    # groups on two streams)
+    # that launches do not overlap and their durations add up (the timed steps overlap the batch
+    # groups on their streams)
     import atomic_gdn2.pipeline as _pipe
     nstreams = _pipe._nstreams
     _pipe._nstreams = 1
