@@ -9,6 +9,8 @@ import ctypes
 import pathlib
 import threading
 
+from .precision import ENUM
+
 _LIB_PATH = pathlib.Path(__file__).resolve().parent / "_lib" / "libgdn2_b200.so"
 _lock = threading.Lock()
 _lib = None
@@ -16,7 +18,7 @@ _lib = None
 # gdn2_status
 OK, ERR_INVALID_ARGUMENT, ERR_CUDA, ERR_UNSUPPORTED = 0, 1, 2, 3
 # gdn2_precision
-PREC = {"highest": 0, "bf16x3": 1, "default": 2, "tf32": 3}
+PREC = ENUM
 # gdn2_dtype
 F32, BF16 = 0, 1
 # device status bits
@@ -35,7 +37,8 @@ class Gdn2Desc(ctypes.Structure):
     ]
 
 
-EXPORTS = ("gdn2_residual_bytes", "gdn2_bwd_workspace_bytes", "gdn2_fwd", "gdn2_bwd",
+EXPORTS = ("gdn2_residual_bytes", "gdn2_fwd_workspace_bytes", "gdn2_bwd_workspace_bytes", "gdn2_fwd", "gdn2_bwd",
+           "gdn2_set_batch_groups", "gdn2_get_batch_groups",
            "gdn2_status_string", "gdn2_selftest_gemm", "gdn2_profile_enable", "gdn2_profile_collect",
            "gdn2_fwd_noalloc", "gdn2_prologue_fwd", "gdn2_prologue_bwd", "gdn2_selftest_engine",
            "gdn2_selftest_wait_timeout")
@@ -47,10 +50,16 @@ def _declare(lib):
     P = ctypes.c_void_p
     lib.gdn2_residual_bytes.restype = ctypes.c_size_t
     lib.gdn2_residual_bytes.argtypes = [ctypes.POINTER(Gdn2Desc)]
+    lib.gdn2_fwd_workspace_bytes.restype = ctypes.c_size_t
+    lib.gdn2_fwd_workspace_bytes.argtypes = [ctypes.POINTER(Gdn2Desc)]
     lib.gdn2_bwd_workspace_bytes.restype = ctypes.c_size_t
     lib.gdn2_bwd_workspace_bytes.argtypes = [ctypes.POINTER(Gdn2Desc)]
     lib.gdn2_fwd.restype = ctypes.c_int
-    lib.gdn2_fwd.argtypes = [ctypes.POINTER(Gdn2Desc)] + [P] * 12
+    lib.gdn2_fwd.argtypes = [ctypes.POINTER(Gdn2Desc)] + [P] * 13
+    lib.gdn2_set_batch_groups.restype = ctypes.c_int32
+    lib.gdn2_set_batch_groups.argtypes = [ctypes.c_int32]
+    lib.gdn2_get_batch_groups.restype = ctypes.c_int32
+    lib.gdn2_get_batch_groups.argtypes = []
     lib.gdn2_bwd.restype = ctypes.c_int
     lib.gdn2_bwd.argtypes = [ctypes.POINTER(Gdn2Desc)] + [P] * 19
     lib.gdn2_status_string.restype = ctypes.c_char_p
@@ -73,6 +82,16 @@ def _declare(lib):
     lib.gdn2_prologue_bwd.restype = ctypes.c_int
     lib.gdn2_prologue_bwd.argtypes = [P, I64, I64, I64, I64, ctypes.c_float, ctypes.c_int32] + [P] * 8
     return lib
+
+
+def set_batch_groups(n: int) -> int:
+    """Concurrent batch groups of each gdn2_fwd / gdn2_bwd call (1..8; results do not depend on it).
+    Returns the previous value."""
+    return int(load().gdn2_set_batch_groups(int(n)))
+
+
+def batch_groups() -> int:
+    return int(load().gdn2_get_batch_groups())
 
 
 def profile_enable(on: bool) -> None:

@@ -25,9 +25,9 @@ from __future__ import annotations
 
 import dataclasses as dc
 
+from .precision import DOT_MODES, EXTRA_DOT_MODES  # the mode table
+
 MB = 1024 * 1024
-DOT_MODES = ("highest", "bf16x3", "default")
-EXTRA_DOT_MODES = ("tf32",)          # B200-only mode (1 x kind::tf32)
 DIAGS = ("btl", "lean")
 BTL_HARD_LIMIT = 88.0     # exp overflow of one BTL leg (f32)
 BTL_WARN = 60.0

@@ -14,9 +14,17 @@ place of jax.custom_vjp:
   result is bit-identical to one launch sequence per segment, because the scans store and reload
   the carried state unchanged at a boundary and every other kernel is chunk-local.  Residuals
   are the same size either way (the reference also keeps every segment's residuals);
-* the batch is split into GDN2_STREAMS (default 4) contiguous groups whose launch sequences run
-  on separate streams (joined before returning), so one group's low-occupancy scans and
-  last-wave tails overlap the other group's chunk kernels;
+* inside the library the heads are split into batch groups (gdn2_set_batch_groups, default 4,
+  environment GDN2_STREAMS) whose launch sequences run on forked side streams joined back to the
+  caller's stream, so one group's low-occupancy scans and last-wave tails overlap the other
+  groups' chunk kernels; the host issues one C call per segment group in each direction;
+* device status: every call ORs its status bits (a bounded on-chip wait that ran out, a positive
+  gate) into one persistent status word per device.  By default the word is checked without
+  stalling the host: after each call an asynchronous copy of it goes to pinned host memory, and a
+  later call raises once that copy has landed with a bit set (last_status() reads the word).  GDN2_CHECK=sync
+  (or set_checks(True)) synchronises after every call and raises at once; GDN2_CHECK=0 turns the
+  checks off.  Nothing is checked while a stream is being captured into a CUDA graph (the word
+  still collects the replays' bits: read it with last_status());
 * backward returns gradients for all seven arguments, each in its input's dtype after the final
   sanitize at 1e4 (pipeline.py:11-14, 38-47); do and dh_final are taken as fp32 (pipeline.py:42).
 
@@ -25,6 +33,7 @@ include/gdn2_b200.h.  PyTorch only provides device memory, streams and autograd 
 """
 from __future__ import annotations
 
+import collections
 import ctypes
 import os
 
@@ -32,47 +41,115 @@ import torch
 
 from . import _lib
 from .config import BLRConfig
+from .precision import sanitize
 
 _FINAL_CLIP = 1e4
-_checks = os.environ.get("GDN2_CHECK", "1") != "0"
 _group_bytes = int(os.environ.get("GDN2_SEGMENT_GROUP_BYTES", str(4 << 30)))
 
 
-def _segment_groups(lib, cfg, scale, B, H, D, sb, sh, dtype, nc):
-    """Chunk ranges [s, e) of the launches: whole segments of cfg.max_chunks_per_call chunks,
-    grouped while the group's backward workspace fits the byte budget (at least one segment)."""
-    seg = cfg.max_chunks_per_call
-    one = _make_desc(cfg, scale, B, H, min(nc, seg) * cfg.bt, D, sb, sh, dtype)
-    ws_seg = max(1, lib.gdn2_bwd_workspace_bytes(ctypes.byref(one)))
-    per_group = max(1, _group_bytes // ws_seg) * seg
-    return [(s, min(nc, s + per_group)) for s in range(0, nc, per_group)]
+def _mode_from_env() -> str:
+    v = os.environ.get("GDN2_CHECK", "async").strip().lower()
+    if v in ("0", "off", "false", "no"):
+        return "off"
+    if v in ("sync", "2"):
+        return "sync"
+    return "async"
 
 
-def set_checks(enabled: bool) -> None:
-    """Synchronise after every launch and turn device status bits into exceptions (default on;
-    environment GDN2_CHECK=0 turns it off).  With checks off, read `last_status()` yourself."""
-    global _checks
-    _checks = bool(enabled)
+_check_mode = _mode_from_env()
 
 
-_last_status: torch.Tensor | None = None
+def set_checks(enabled) -> None:
+    """Device status checks: True or "sync" (synchronise after every call and raise at once),
+    "async" (the default: raise at a later call once the status copy has landed, without
+    stalling the host), False or "off" (no checks; read last_status() yourself)."""
+    global _check_mode
+    if enabled is True or enabled == "sync":
+        _check_mode = "sync"
+    elif enabled is False or enabled in ("off", None):
+        _check_mode = "off"
+    elif enabled == "async":
+        _check_mode = "async"
+    else:
+        raise ValueError(f"set_checks: {enabled!r} is not True, False, 'sync', 'async' or 'off'")
+
+
+class _DevStatus:
+    """The persistent status word of one device and the in-flight asynchronous copies of it."""
+
+    NSLOT = 16
+
+    def __init__(self, dev: torch.device):
+        self.word = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.host = torch.zeros(self.NSLOT, dtype=torch.int32, pin_memory=True)
+        self.pending = collections.deque()      # (event, slot, what)
+        self.next_slot = 0
+
+
+_status = {}
+
+
+def _dev_status(dev: torch.device) -> _DevStatus:
+    st = _status.get(dev.index)
+    if st is None:
+        st = _status[dev.index] = _DevStatus(dev)
+    return st
 
 
 def last_status() -> int:
-    """Device status bits of the most recent call (synchronises)."""
-    return 0 if _last_status is None else int(_last_status.item())
+    """Status bits collected on the current device since they were last raised (synchronises)."""
+    if not torch.cuda.is_available():
+        return 0
+    st = _status.get(torch.cuda.current_device())
+    return 0 if st is None else int(st.word.item())
 
 
-def _raise_on_status(st: torch.Tensor, what: str):
-    code = int(st.item())
-    if code == 0:
-        return
+def _status_message(code: int, what: str) -> str:
     msgs = []
     if code & _lib.DEV_TIMEOUT:
         msgs.append("an on-chip wait timed out (results invalid)")
     if code & _lib.DEV_POSITIVE_GATE:
         msgs.append("g > 0 seen: outside domain I-1 (g <= 0)")
-    raise RuntimeError(f"{what}: " + "; ".join(msgs))
+    if not msgs:
+        msgs.append(f"device status {code:#x}")
+    return f"{what}: " + "; ".join(msgs)
+
+
+def _raise_on_status(st: torch.Tensor, what: str):
+    """Raise if the status word `st` has a bit set (synchronises)."""
+    code = int(st.item())
+    if code:
+        raise RuntimeError(_status_message(code, what))
+
+
+def _after_call(st: _DevStatus, what: str) -> None:
+    """Device status check after the launches of one call (see the module docstring)."""
+    if _check_mode == "off" or torch.cuda.is_current_stream_capturing():
+        return
+    if _check_mode == "sync":
+        code = int(st.word.item())
+        if code:
+            st.word.zero_()
+            st.pending.clear()
+            raise RuntimeError(_status_message(code, what))
+        return
+    # async: report copies that have landed, then queue this call's copy
+    while st.pending and st.pending[0][0].query():
+        _, slot, w = st.pending.popleft()
+        code = int(st.host[slot])
+        if code:
+            st.word.zero_()
+            st.pending.clear()
+            raise RuntimeError(_status_message(code, f"{w} (reported at a later call)"))
+    if len(st.pending) == st.NSLOT:          # every slot in flight: wait for the oldest
+        st.pending[0][0].synchronize()
+        return _after_call(st, what)
+    slot = st.next_slot
+    st.next_slot = (slot + 1) % st.NSLOT
+    st.host[slot:slot + 1].copy_(st.word, non_blocking=True)
+    ev = torch.cuda.Event()
+    ev.record()
+    st.pending.append((ev, slot, what))
 
 
 def _ptr(t):
@@ -81,13 +158,6 @@ def _ptr(t):
 
 def _stream():
     return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-
-
-class _Segment:
-    """Static description of one segment launch: chunk range and C descriptor."""
-
-    def __init__(self, desc: _lib.Gdn2Desc, a: int, c: int):
-        self.desc, self.a, self.c = desc, a, c
 
 
 def _make_desc(cfg: BLRConfig, scale: float, B, H, Lseg, D, stride_b, stride_h, dtype) -> _lib.Gdn2Desc:
@@ -103,34 +173,49 @@ def _make_desc(cfg: BLRConfig, scale: float, B, H, Lseg, D, stride_b, stride_h, 
     return d
 
 
+class _Seg:
+    """One launch of a call: chunk range [a, c) and its descriptor with the buffer sizes."""
+
+    __slots__ = ("a", "c", "desc", "ref", "res_bytes", "fws_bytes", "bws_bytes")
+
+    def __init__(self, lib, cfg, scale, B, H, D, sb, sh, dtype, a, c):
+        self.a, self.c = a, c
+        self.desc = _make_desc(cfg, scale, B, H, (c - a) * cfg.bt, D, sb, sh, dtype)
+        self.ref = ctypes.byref(self.desc)
+        self.res_bytes = lib.gdn2_residual_bytes(self.ref)
+        if self.res_bytes == 0:
+            _lib.check(_lib.ERR_INVALID_ARGUMENT, "gdn2_residual_bytes")
+        self.fws_bytes = lib.gdn2_fwd_workspace_bytes(self.ref)
+        self.bws_bytes = lib.gdn2_bwd_workspace_bytes(self.ref)
+
+
+_plans = {}
+
+
+def _plan(lib, cfg, scale, B, H, D, sb, sh, dtype, nc):
+    """The call's segment launches (cached per configuration and shape): whole segments of
+    cfg.max_chunks_per_call chunks, consecutive segments grouped into one launch sequence while the
+    group's backward workspace fits GDN2_SEGMENT_GROUP_BYTES (at least one segment)."""
+    key = (cfg, scale, B, H, D, sb, sh, dtype, nc)
+    plan = _plans.get(key)
+    if plan is None:
+        seg = cfg.max_chunks_per_call
+        one = _Seg(lib, cfg, scale, B, H, D, sb, sh, dtype, 0, min(nc, seg))
+        per_group = max(1, _group_bytes // max(1, one.bws_bytes)) * seg
+        plan = [_Seg(lib, cfg, scale, B, H, D, sb, sh, dtype, s, min(nc, s + per_group))
+                for s in range(0, nc, per_group)]
+        if len(_plans) > 256:
+            _plans.clear()
+        _plans[key] = plan
+    return plan
+
+
 def _fin(x: torch.Tensor, dt: torch.dtype, cfg: BLRConfig) -> torch.Tensor:
     """pipeline.py:11-14: the kernels already sanitize at cfg.clip and write in the input dtype;
     re-sanitize only when cfg.clip is looser than the final 1e4 bound."""
     if cfg.clip <= _FINAL_CLIP and x.dtype == dt:
         return x
-    return torch.nan_to_num(x.float().clamp(-_FINAL_CLIP, _FINAL_CLIP), nan=0.0,
-                            posinf=_FINAL_CLIP, neginf=-_FINAL_CLIP).to(dt)
-
-
-_nstreams = max(1, int(os.environ.get("GDN2_STREAMS", "4")))
-_side = {}
-
-
-def _streams(dev: torch.device, n: int):
-    """n side streams of a device (created once): batch groups run on them concurrently."""
-    lst = _side.setdefault(dev.index, [])
-    while len(lst) < n:
-        lst.append(torch.cuda.Stream(device=dev))
-    return lst[:n]
-
-
-def _batch_groups(B: int):
-    """Contiguous batch ranges [b0, b1) processed as independent launch sequences.  Their kernels
-    overlap on the GPU: one group's low-occupancy scans and last-wave tails run beside the other
-    group's chunk kernels (the batch entries are independent recurrences)."""
-    n = min(_nstreams, B)
-    step = -(-B // n)
-    return [(b0, min(B, b0 + step)) for b0 in range(0, B, step)]
+    return sanitize(x.float(), _FINAL_CLIP).to(dt)
 
 
 class _GDN2(torch.autograd.Function):
@@ -144,7 +229,7 @@ class _GDN2(torch.autograd.Function):
         # with one stride pair (views of longer sequences are consumed without copies)
         o = torch.empty_strided((B, H, L, D), q.stride(), dtype=torch.float32, device=dev)
         h_final = torch.empty((B, H, D, D), dtype=torch.float32, device=dev)
-        status = torch.zeros(1, dtype=torch.int32, device=dev)
+        st = _dev_status(dev)
         # strides of size-1 dims are never used to form an address; give them canonical values
         sb, sh = q.stride(0), q.stride(1)
         if H == 1:
@@ -152,42 +237,24 @@ class _GDN2(torch.autograd.Function):
         if B == 1:
             sb = max(sb, H * sh)
         el = q.element_size()
-        groups = _batch_groups(B)
-        main = torch.cuda.current_stream(dev)
-        streams = _streams(dev, len(groups)) if len(groups) > 1 else [main]
-        plan = []
-        for (b0, b1), st in zip(groups, streams):
-            if st is not main:
-                st.wait_stream(main)
-            Bg = b1 - b0
-            with torch.cuda.stream(st):
-                h = None if h0 is None else h0[b0:b1]
-                segs = []
-                seg_groups = _segment_groups(lib, cfg, scale, Bg, H, D, sb, sh, q.dtype, nc)
-                for si, (s, e) in enumerate(seg_groups):
-                    desc = _make_desc(cfg, scale, Bg, H, (e - s) * cfg.bt, D, sb, sh, q.dtype)
-                    nbytes = lib.gdn2_residual_bytes(ctypes.byref(desc))
-                    if nbytes == 0:
-                        _lib.check(_lib.ERR_INVALID_ARGUMENT, "gdn2_residual_bytes")
-                    res = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-                    last = si == len(seg_groups) - 1
-                    h_out = h_final[b0:b1] if last else torch.empty((Bg, H, D, D), dtype=torch.float32, device=dev)
-                    off = b0 * sb + s * cfg.bt * D
-                    ins = [ctypes.c_void_p(t.data_ptr() + off * el) for t in (q, k, v, w, b, g)]
-                    rc = lib.gdn2_fwd(ctypes.byref(desc), *ins, _ptr(h), ctypes.c_void_p(o.data_ptr() + off * 4),
-                                      _ptr(h_out), _ptr(res), _ptr(status), _stream())
-                    _lib.check(rc, "gdn2_fwd")
-                    segs.append((_Segment(desc, s, e), res if need_res else None))
-                    h = h_out
-            plan.append((b0, b1, segs))
-        for st in streams:
-            if st is not main:
-                main.wait_stream(st)
-        global _last_status
-        _last_status = status
-        if _checks:
-            _raise_on_status(status, "gdn2_fwd")
-        ctx.cfg, ctx.plan = cfg, plan
+        stream = _stream()
+        h = h0
+        saved = []
+        plan = _plan(lib, cfg, scale, B, H, D, sb, sh, q.dtype, nc)
+        for si, sg in enumerate(plan):
+            res = torch.empty(sg.res_bytes, dtype=torch.uint8, device=dev)
+            fws = torch.empty(sg.fws_bytes, dtype=torch.uint8, device=dev)  # free once the call returns
+            last = si == len(plan) - 1
+            h_out = h_final if last else torch.empty((B, H, D, D), dtype=torch.float32, device=dev)
+            off = sg.a * cfg.bt * D
+            ins = [ctypes.c_void_p(t.data_ptr() + off * el) for t in (q, k, v, w, b, g)]
+            rc = lib.gdn2_fwd(sg.ref, *ins, _ptr(h), ctypes.c_void_p(o.data_ptr() + off * 4), _ptr(h_out),
+                              _ptr(res), _ptr(fws), _ptr(st.word), stream)
+            _lib.check(rc, "gdn2_fwd")
+            saved.append(res if need_res else None)
+            h = h_out
+        _after_call(st, "gdn2_fwd")
+        ctx.cfg, ctx.plan, ctx.res = cfg, plan, saved
         ctx.h0_dtype = None if h0 is None else h0.dtype
         ctx.save_for_backward(q, k, v, w, b, g)
         return o, h_final
@@ -199,48 +266,37 @@ class _GDN2(torch.autograd.Function):
         q, k, v, w, b, g = ctx.saved_tensors
         B, H, L, D = q.shape
         dev = q.device
-        if any(res is None for _, _, segs in ctx.plan for _, res in segs):
+        if any(res is None for res in ctx.res):
             raise RuntimeError("gdn2: backward through a call made without gradient tracking")
         # every (B,H,L,D) tensor of a call shares the inputs' strides (see forward)
-        do_s = torch.empty_strided((B, H, L, D), q.stride(), dtype=torch.float32, device=dev)
-        if do is None:
-            do_s.zero_()
+        if do is not None and do.dtype == torch.float32 and do.stride() == q.stride():
+            do_s = do
         else:
-            do_s.copy_(do)
+            do_s = torch.empty_strided((B, H, L, D), q.stride(), dtype=torch.float32, device=dev)
+            if do is None:
+                do_s.zero_()
+            else:
+                do_s.copy_(do)
         dhf32 = None if dhf is None else dhf.to(torch.float32).contiguous()
         grads = [torch.empty_strided(t.shape, q.stride(), dtype=t.dtype, device=dev) for t in (q, k, v, w, b, g)]
         dh0_all = torch.empty((B, H, D, D), dtype=torch.float32, device=dev)
-        status = torch.zeros(1, dtype=torch.int32, device=dev)
+        st = _dev_status(dev)
         el = q.element_size()
-        sb = ctx.plan[0][2][0][0].desc.stride_b
-        main = torch.cuda.current_stream(dev)
-        streams = _streams(dev, len(ctx.plan)) if len(ctx.plan) > 1 else [main]
-        for (b0, b1, segs), st in zip(ctx.plan, streams):
-            if st is not main:
-                st.wait_stream(main)
-            Bg = b1 - b0
-            with torch.cuda.stream(st):
-                dh = None if dhf32 is None else dhf32[b0:b1]
-                for si, (sgm, res) in enumerate(reversed(segs)):
-                    off = b0 * sb + sgm.a * cfg.bt * D
-                    ws = torch.empty(lib.gdn2_bwd_workspace_bytes(ctypes.byref(sgm.desc)), dtype=torch.uint8,
-                                     device=dev)
-                    first = si == len(segs) - 1
-                    dh0 = dh0_all[b0:b1] if first else torch.empty((Bg, H, D, D), dtype=torch.float32, device=dev)
-                    ins = [ctypes.c_void_p(t.data_ptr() + off * el) for t in (q, k, v, w, b, g)]
-                    outs = [ctypes.c_void_p(t.data_ptr() + off * el) for t in grads]
-                    rc = lib.gdn2_bwd(ctypes.byref(sgm.desc), *ins, _ptr(res),
-                                      ctypes.c_void_p(do_s.data_ptr() + off * 4), _ptr(dh), *outs, _ptr(dh0), _ptr(ws),
-                                      _ptr(status), _stream())
-                    _lib.check(rc, "gdn2_bwd")
-                    dh = dh0
-        for st in streams:
-            if st is not main:
-                main.wait_stream(st)
-        global _last_status
-        _last_status = status
-        if _checks:
-            _raise_on_status(status, "gdn2_bwd")
+        stream = _stream()
+        dh = dhf32
+        n = len(ctx.plan)
+        for si in range(n - 1, -1, -1):
+            sg, res = ctx.plan[si], ctx.res[si]
+            off = sg.a * cfg.bt * D
+            ws = torch.empty(sg.bws_bytes, dtype=torch.uint8, device=dev)
+            dh0 = dh0_all if si == 0 else torch.empty((B, H, D, D), dtype=torch.float32, device=dev)
+            ins = [ctypes.c_void_p(t.data_ptr() + off * el) for t in (q, k, v, w, b, g)]
+            outs = [ctypes.c_void_p(t.data_ptr() + off * el) for t in grads]
+            rc = lib.gdn2_bwd(sg.ref, *ins, _ptr(res), ctypes.c_void_p(do_s.data_ptr() + off * 4), _ptr(dh), *outs,
+                              _ptr(dh0), _ptr(ws), _ptr(st.word), stream)
+            _lib.check(rc, "gdn2_bwd")
+            dh = dh0
+        _after_call(st, "gdn2_bwd")
         grads = [_fin(gr, t.dtype, cfg) for gr, t in zip(grads, (q, k, v, w, b, g))]
         dh0 = None
         if ctx.h0_dtype is not None and ctx.needs_input_grad[9]:

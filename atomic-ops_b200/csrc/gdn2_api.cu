@@ -1,4 +1,6 @@
 // C-ABI entry points: argument validation, residual / workspace layout and kernel orchestration.
+#include <atomic>
+#include <cstdlib>
 #include <mutex>
 #include <vector>
 
@@ -18,9 +20,11 @@ extern "C" const char* gdn2_status_string(gdn2_status status) {
 
 namespace {
 
-bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
-bool aligned256(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 255u) == 0; }
 bool mode_ok(int32_t m) { return m >= GDN2_PREC_HIGHEST && m <= GDN2_PREC_TF32; }
+
+}  // namespace
+
+namespace gdn2 {
 
 // Shape / config validation shared by every entry point (the reference raises ValueError for a
 // sequence length that is not a multiple of bt, pipeline.py:54-55, and for bad configs,
@@ -41,6 +45,13 @@ gdn2_status check_desc(const gdn2_desc* d) {
   if (d->bt != kT || d->D != kD) return GDN2_ERR_UNSUPPORTED;
   return GDN2_OK;
 }
+
+}  // namespace gdn2
+
+namespace {
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+bool aligned256(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 255u) == 0; }
 
 OpParams make_params(const gdn2_desc* d, const void* q, const void* k, const void* v, const void* w,
                      const void* b, const void* g, void* residual, uint32_t* status) {
@@ -121,9 +132,93 @@ extern "C" int32_t gdn2_profile_collect(float* ms, int32_t* counts, int32_t n) {
   return total;
 }
 
+namespace {
+
+// ---------------------------------------------------------------------------------------------
+// Batch groups.  The heads of a call are split into up to `groups` contiguous ranges whose launch
+// sequences run on library-owned side streams, forked from and joined back to the caller's stream
+// with events (so the call stays ordered on the caller's stream, and stream capture into a CUDA
+// graph records the fork and the join).  One group's low-occupancy state scan and its chunk
+// kernels' last-wave tails then overlap the other groups' chunk kernels (every head is an
+// independent recurrence).
+// ---------------------------------------------------------------------------------------------
+constexpr int kMaxGroups = 8;
+constexpr int kMaxDevs = 64;
+
+int initial_groups() {
+  const char* e = std::getenv("GDN2_STREAMS");
+  int n = e ? std::atoi(e) : 4;
+  return n < 1 ? 1 : (n > kMaxGroups ? kMaxGroups : n);
+}
+std::atomic<int> g_groups{initial_groups()};
+
+struct DevStreams {
+  std::mutex mu;
+  bool ready = false;
+  cudaStream_t side[kMaxGroups] = {};
+  cudaEvent_t fork = nullptr;
+  cudaEvent_t join[kMaxGroups] = {};
+};
+DevStreams g_dev_streams[kMaxDevs];
+
+// Creates the side streams and events of the current device on first use (outside any capture).
+DevStreams* dev_streams(cudaStream_t caller) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevs) return nullptr;
+  DevStreams& ds = g_dev_streams[dev];
+  std::lock_guard<std::mutex> g(ds.mu);
+  if (ds.ready) return &ds;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(caller, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) return nullptr;
+  bool ok = cudaEventCreateWithFlags(&ds.fork, cudaEventDisableTiming) == cudaSuccess;
+  for (int i = 0; ok && i < kMaxGroups; ++i) {
+    ok = cudaStreamCreateWithFlags(&ds.side[i], cudaStreamNonBlocking) == cudaSuccess &&
+         cudaEventCreateWithFlags(&ds.join[i], cudaEventDisableTiming) == cudaSuccess;
+  }
+  ds.ready = ok;
+  return ok ? &ds : nullptr;
+}
+
+// Runs launch(group, first_head, n_heads, stream) for every group of the call's BH heads: on the
+// caller's stream for a single group, else on forked side streams.
+template <class F>
+gdn2_status run_groups(int BH, cudaStream_t st, F launch) {
+  int G = g_groups.load(std::memory_order_relaxed);
+  if (G > BH) G = BH;
+  DevStreams* ds = G > 1 ? dev_streams(st) : nullptr;
+  if (!ds) G = 1;
+  if (G == 1) return launch(0, BH, st) == cudaSuccess ? GDN2_OK : GDN2_ERR_CUDA;
+  std::lock_guard<std::mutex> g(ds->mu);  // the fork / join events are shared by the device's calls
+  if (cudaEventRecord(ds->fork, st) != cudaSuccess) return GDN2_ERR_CUDA;
+  gdn2_status s = GDN2_OK;
+  for (int i = 0; i < G; ++i) {
+    const int h0 = (int)((long long)BH * i / G), h1 = (int)((long long)BH * (i + 1) / G);
+    if (cudaStreamWaitEvent(ds->side[i], ds->fork, 0) != cudaSuccess) return GDN2_ERR_CUDA;
+    if (s == GDN2_OK && launch(h0, h1 - h0, ds->side[i]) != cudaSuccess) s = GDN2_ERR_CUDA;
+    // joined even after a failed launch, so that the caller's stream (and a capture) stays whole
+    if (cudaEventRecord(ds->join[i], ds->side[i]) != cudaSuccess) return GDN2_ERR_CUDA;
+    if (cudaStreamWaitEvent(st, ds->join[i], 0) != cudaSuccess) return GDN2_ERR_CUDA;
+  }
+  return s;
+}
+
+}  // namespace
+
+extern "C" int32_t gdn2_set_batch_groups(int32_t n) {
+  const int v = n < 1 ? 1 : (n > kMaxGroups ? kMaxGroups : n);
+  return g_groups.exchange(v);
+}
+
+extern "C" int32_t gdn2_get_batch_groups(void) { return g_groups.load(); }
+
 extern "C" size_t gdn2_residual_bytes(const gdn2_desc* d) {
   if (check_desc(d) != GDN2_OK) return 0;
   return res_layout(d->B * d->H, d->L / d->bt, mode_from_enum(d->dot_mode)).total;
+}
+
+extern "C" size_t gdn2_fwd_workspace_bytes(const gdn2_desc* d) {
+  if (check_desc(d) != GDN2_OK) return 0;
+  return res_layout(d->B * d->H, d->L / d->bt, mode_from_enum(d->dot_mode)).ws_total;
 }
 
 extern "C" size_t gdn2_bwd_workspace_bytes(const gdn2_desc* d) {
@@ -133,40 +228,47 @@ extern "C" size_t gdn2_bwd_workspace_bytes(const gdn2_desc* d) {
 
 extern "C" gdn2_status gdn2_fwd(const gdn2_desc* d, const void* q, const void* k, const void* v, const void* w,
                                 const void* b, const void* g, const float* h0, float* o, float* h_final,
-                                void* residual, uint32_t* dev_status, void* stream) {
+                                void* residual, void* workspace, uint32_t* dev_status, void* stream) {
   gdn2_status s = check_desc(d);
   if (s != GDN2_OK) return s;
   const void* ins[] = {q, k, v, w, b, g, o, h_final};
   for (const void* x : ins)
     if (!x || !aligned16(x)) return GDN2_ERR_INVALID_ARGUMENT;
-  if ((h0 && !aligned16(h0)) || !residual || !aligned256(residual) || !dev_status) return GDN2_ERR_INVALID_ARGUMENT;
+  if ((h0 && !aligned16(h0)) || !residual || !aligned256(residual) || !workspace || !aligned256(workspace) ||
+      !dev_status)
+    return GDN2_ERR_INVALID_ARGUMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool bf16 = d->in_dtype == GDN2_BF16;
-  const OpParams p = make_params(d, q, k, v, w, b, g, residual, dev_status);
-  const int BH = d->B * d->H, NC = p.NC;
+  const OpParams base = make_params(d, q, k, v, w, b, g, residual, dev_status);
+  const int BH = d->B * d->H, NC = base.NC;
 
-  if (timed(GDN2_K_FWD_INTRA, st, [&] { return launch_fwd_intra(p, bf16, BH * NC, st); }) != cudaSuccess)
-    return GDN2_ERR_CUDA;
+  ScanParams sb{};
+  sb.img = static_cast<uint8_t*>(workspace) + base.rl.mf;
+  sb.img_stride = base.rl.mf_stride;
+  sb.add = reinterpret_cast<const float*>(static_cast<uint8_t*>(workspace) + base.rl.bc);
+  sb.state_in = h0;
+  sb.states = reinterpret_cast<float*>(base.res + base.rl.hs);
+  sb.states_per_head = NC + 1;
+  sb.store_final_state = 1;
+  sb.final_out = h_final;
+  sb.NC = NC;
+  sb.mode = d->dot_mode;
+  sb.reverse = 0;
+  sb.clip = d->clip;
+  sb.status = dev_status;
 
-  ScanParams sp{};
-  sp.img = p.res + p.rl.mf;
-  sp.img_stride = p.rl.mf_stride;
-  sp.add = reinterpret_cast<const float*>(p.res + p.rl.bc);
-  sp.state_in = h0;
-  sp.states = reinterpret_cast<float*>(p.res + p.rl.hs);
-  sp.states_per_head = NC + 1;
-  sp.store_final_state = 1;
-  sp.final_out = h_final;
-  sp.NC = NC;
-  sp.mode = d->dot_mode;
-  sp.reverse = 0;
-  sp.clip = d->clip;
-  sp.status = dev_status;
-  if (timed(GDN2_K_FWD_SCAN, st, [&] { return launch_scan(sp, BH, st); }) != cudaSuccess) return GDN2_ERR_CUDA;
-
-  if (timed(GDN2_K_FWD_OUT, st, [&] { return launch_fwd_out(p, bf16, o, BH * NC, st); }) != cudaSuccess)
-    return GDN2_ERR_CUDA;
-  return GDN2_OK;
+  return run_groups(BH, st, [&](int h_first, int nh, cudaStream_t gs) -> cudaError_t {
+    OpParams p = base;
+    p.fws = static_cast<uint8_t*>(workspace);
+    p.ch0 = h_first * NC;
+    cudaError_t e = timed(GDN2_K_FWD_INTRA, gs, [&] { return launch_fwd_intra(p, bf16, nh * NC, gs); });
+    if (e != cudaSuccess) return e;
+    ScanParams sp = sb;
+    sp.bh0 = h_first;
+    e = timed(GDN2_K_FWD_SCAN, gs, [&] { return launch_scan(sp, nh, gs); });
+    if (e != cudaSuccess) return e;
+    return timed(GDN2_K_FWD_OUT, gs, [&] { return launch_fwd_out(p, bf16, o, nh * NC, gs); });
+  });
 }
 
 extern "C" gdn2_status gdn2_bwd(const gdn2_desc* d, const void* q, const void* k, const void* v, const void* w,
@@ -183,34 +285,38 @@ extern "C" gdn2_status gdn2_bwd(const gdn2_desc* d, const void* q, const void* k
     return GDN2_ERR_INVALID_ARGUMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool bf16 = d->in_dtype == GDN2_BF16;
-  BwdParams bp{};
-  bp.op = make_params(d, q, k, v, w, b, g, const_cast<void*>(residual), dev_status);
-  bp.d_o = d_o;
-  bp.dq = dq; bp.dk = dk; bp.dv = dv; bp.dw = dw; bp.db = db; bp.dg = dg;
-  bp.ws = static_cast<uint8_t*>(workspace);
-  const int BH = d->B * d->H, NC = bp.op.NC;
-  bp.wl = ws_layout(BH, NC, mode_from_enum(d->b3_dot_mode));
+  BwdParams base{};
+  base.op = make_params(d, q, k, v, w, b, g, const_cast<void*>(residual), dev_status);
+  base.d_o = d_o;
+  base.dq = dq; base.dk = dk; base.dv = dv; base.dw = dw; base.db = db; base.dg = dg;
+  base.ws = static_cast<uint8_t*>(workspace);
+  const int BH = d->B * d->H, NC = base.op.NC;
+  base.wl = ws_layout(BH, NC, mode_from_enum(d->b3_dot_mode));
 
-  if (timed(GDN2_K_BWD_PRE, st, [&] { return launch_bwd_pre(bp, bf16, BH * NC, st); }) != cudaSuccess)
-    return GDN2_ERR_CUDA;
+  ScanParams sb{};
+  sb.img = base.ws + base.wl.mb;
+  sb.img_stride = base.wl.mb_stride;
+  sb.add = reinterpret_cast<const float*>(base.ws + base.wl.cc);
+  sb.state_in = d_hfinal;
+  sb.states = reinterpret_cast<float*>(base.ws + base.wl.dhs);
+  sb.states_per_head = NC;
+  sb.store_final_state = 0;
+  sb.final_out = dh0;
+  sb.NC = NC;
+  sb.mode = d->b3_dot_mode;
+  sb.reverse = 1;
+  sb.clip = d->clip;
+  sb.status = dev_status;
 
-  ScanParams sp{};
-  sp.img = bp.ws + bp.wl.mb;
-  sp.img_stride = bp.wl.mb_stride;
-  sp.add = reinterpret_cast<const float*>(bp.ws + bp.wl.cc);
-  sp.state_in = d_hfinal;
-  sp.states = reinterpret_cast<float*>(bp.ws + bp.wl.dhs);
-  sp.states_per_head = NC;
-  sp.store_final_state = 0;
-  sp.final_out = dh0;
-  sp.NC = NC;
-  sp.mode = d->b3_dot_mode;
-  sp.reverse = 1;
-  sp.clip = d->clip;
-  sp.status = dev_status;
-  if (timed(GDN2_K_BWD_SCAN, st, [&] { return launch_scan(sp, BH, st); }) != cudaSuccess) return GDN2_ERR_CUDA;
-
-  if (timed(GDN2_K_BWD_INTRA, st, [&] { return launch_bwd_intra(bp, bf16, BH * NC, st); }) != cudaSuccess)
-    return GDN2_ERR_CUDA;
-  return GDN2_OK;
+  return run_groups(BH, st, [&](int h_first, int nh, cudaStream_t gs) -> cudaError_t {
+    BwdParams bp = base;
+    bp.op.ch0 = h_first * NC;
+    cudaError_t e = timed(GDN2_K_BWD_PRE, gs, [&] { return launch_bwd_pre(bp, bf16, nh * NC, gs); });
+    if (e != cudaSuccess) return e;
+    ScanParams sp = sb;
+    sp.bh0 = h_first;
+    e = timed(GDN2_K_BWD_SCAN, gs, [&] { return launch_scan(sp, nh, gs); });
+    if (e != cudaSuccess) return e;
+    return timed(GDN2_K_BWD_INTRA, gs, [&] { return launch_bwd_intra(bp, bf16, nh * NC, gs); });
+  });
 }

@@ -52,7 +52,7 @@ __global__ void __launch_bounds__(kCT, 1) bwd_pre_kernel(const BwdParams P) {
 
   const int tid = threadIdx.x, warp = tid >> 5;
   const int t = crow(), cb = chalf() * 64;
-  const int ch = blockIdx.x, bh = ch / p.NC, c = ch % p.NC;
+  const int ch = p.ch0 + (int)blockIdx.x, bh = ch / p.NC, c = ch % p.NC;
   const long long off = chunk_off(p, bh, c);
   const TIn* q = reinterpret_cast<const TIn*>(p.q) + off;
   const TIn* k = reinterpret_cast<const TIn*>(p.k) + off;
@@ -226,7 +226,7 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
 
   const int tid = threadIdx.x, warp = tid >> 5;
   const int t = crow(), half = chalf(), cb = half * 64;
-  const int ch = blockIdx.x, bh = ch / p.NC, c = ch % p.NC;
+  const int ch = p.ch0 + (int)blockIdx.x, bh = ch / p.NC, c = ch % p.NC;
   if ((reinterpret_cast<const int*>(p.res + p.rl.wide)[ch] != 0) != WIDE) return;
   const long long off = chunk_off(p, bh, c);
   const TIn* q = reinterpret_cast<const TIn*>(p.q) + off;

@@ -105,9 +105,9 @@ __device__ __forceinline__ void fwd_intra_chunk(const OpParams& p, const int ch)
   float* aqk_g = reinterpret_cast<float*>(p.res + p.rl.aqk) + (size_t)ch * mat;
   float* ainv_g = reinterpret_cast<float*>(p.res + p.rl.ainv) + (size_t)ch * mat;
   float* wp_g = reinterpret_cast<float*>(p.res + p.rl.wp) + (size_t)ch * mat;
-  float* u_g = reinterpret_cast<float*>(p.res + p.rl.u) + (size_t)ch * mat;
-  float* bc_g = reinterpret_cast<float*>(p.res + p.rl.bc) + (size_t)ch * mat;
-  uint8_t* mf_g = p.res + p.rl.mf + (size_t)ch * p.rl.mf_stride;
+  float* u_g = reinterpret_cast<float*>(p.fws + p.rl.u) + (size_t)ch * mat;
+  float* bc_g = reinterpret_cast<float*>(p.fws + p.rl.bc) + (size_t)ch * mat;
+  uint8_t* mf_g = p.fws + p.rl.mf + (size_t)ch * p.rl.mf_stride;
 
   const Mode md = mode_from_enum(DOT >= 0 ? DOT : p.dot_mode);
   const Mode ms = mode_from_enum(SOLVE >= 0 ? SOLVE : p.solve_mode);
@@ -377,7 +377,7 @@ __device__ __noinline__ void fwd_intra_wide(const OpParams& p, const int ch) {
 template <class TIn, int DOT, int SOLVE>
 __global__ void __launch_bounds__(kCT, 1) fwd_intra_kernel(const OpParams p) {
   pdl_enter();
-  fwd_intra_chunk<TIn, DOT, SOLVE, false>(p, blockIdx.x);
+  fwd_intra_chunk<TIn, DOT, SOLVE, false>(p, p.ch0 + (int)blockIdx.x);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -395,14 +395,14 @@ __global__ void __launch_bounds__(kCT, 1) fwd_out_kernel(const OpParams p, float
 
   const int tid = threadIdx.x, warp = tid >> 5;
   const int t = crow(), cb = chalf() * 64;
-  const int ch = blockIdx.x, bh = ch / p.NC, c = ch % p.NC;
+  const int ch = p.ch0 + (int)blockIdx.x, bh = ch / p.NC, c = ch % p.NC;
   const long long off = chunk_off(p, bh, c);
   const TIn* q = reinterpret_cast<const TIn*>(p.q) + off;
   const TIn* g = reinterpret_cast<const TIn*>(p.g) + off;
   const size_t mat = (size_t)kT * kD;
   const float* aqk_g = reinterpret_cast<const float*>(p.res + p.rl.aqk) + (size_t)ch * mat;
   const float* wp_g = reinterpret_cast<const float*>(p.res + p.rl.wp) + (size_t)ch * mat;
-  const float* u_g = reinterpret_cast<const float*>(p.res + p.rl.u) + (size_t)ch * mat;
+  const float* u_g = reinterpret_cast<const float*>(p.fws + p.rl.u) + (size_t)ch * mat;
   const float* h_g = reinterpret_cast<const float*>(p.res + p.rl.hs) + ((size_t)bh * (p.NC + 1) + c) * mat;
   float* vn_g = reinterpret_cast<float*>(p.res + p.rl.vnew) + (size_t)ch * mat;
   float* o_g = o_out + off;

@@ -15,9 +15,14 @@ constexpr float kSpanMax = 128.0f;
 __host__ __device__ inline uint32_t image_part_bytes(Mode m) { return m.fmt == kTF32 ? 65536u : 32768u; }
 __host__ __device__ inline uint32_t image_bytes(Mode m) { return image_part_bytes(m) * (m.passes == 3 ? 2u : 1u); }
 
-// Per-call residual layout (byte offsets from the residual base), all regions 256-byte aligned.
+// Per-call layouts of the forward's device memory (byte offsets), all regions 256-byte aligned.
+// Residual (kept from the forward to the backward, read by bwd_pre / bwd_intra): the scores Aqk,
+// the WY inverse A, wp = A (b k e^gc), the state entering every chunk (and h_final), v_new and
+// the per-chunk-head wide-channel flags.  Forward workspace (dead once gdn2_fwd's launches have
+// run): u = A (w v), the state-transition image M and the additive term Bc of the forward scan.
 struct ResLayout {
-  size_t aqk, ainv, wp, u, mf, bc, hs, vnew, wide, total;
+  size_t aqk, ainv, wp, hs, vnew, wide, total;  // residual
+  size_t u, mf, bc, ws_total;                   // forward workspace
   uint32_t mf_stride;  // bytes per chunk-head of the forward state-transition image
 };
 
@@ -31,14 +36,16 @@ __host__ __device__ inline ResLayout res_layout(int BH, int NC, Mode fwd_scan) {
   r.aqk = o; o = align256(o + nch * mat);
   r.ainv = o; o = align256(o + nch * mat);
   r.wp = o; o = align256(o + nch * mat);
-  r.u = o; o = align256(o + nch * mat);
-  r.mf_stride = image_bytes(fwd_scan);
-  r.mf = o; o = align256(o + nch * r.mf_stride);
-  r.bc = o; o = align256(o + nch * mat);
   r.hs = o; o = align256(o + (size_t)BH * (NC + 1) * mat);  // h entering each chunk, then h_final
   r.vnew = o; o = align256(o + nch * mat);
   r.wide = o; o = align256(o + nch * sizeof(int));  // per chunk-head: 1 if it has wide channels
   r.total = o;
+  o = 0;
+  r.u = o; o = align256(o + nch * mat);
+  r.mf_stride = image_bytes(fwd_scan);
+  r.mf = o; o = align256(o + nch * r.mf_stride);
+  r.bc = o; o = align256(o + nch * mat);
+  r.ws_total = o;
   return r;
 }
 
@@ -71,10 +78,12 @@ struct OpParams {
   int dot_mode, solve_mode, b3_mode;
   unsigned* status;
   uint8_t* res;                  // residual base
+  uint8_t* fws;                  // forward workspace base (gdn2_fwd only)
   ResLayout rl;
+  int ch0;                       // first chunk-head of this launch (batch groups split the heads)
 };
 
-// Element offset of chunk c of head (b, h) in a (B,H,L,D) tensor.
+// Element offset of chunk c of head bh = b * H + h in a (B,H,L,D) tensor.
 __device__ __forceinline__ long long chunk_off(const OpParams& p, int bh, int c) {
   const int b = bh / p.H, h = bh % p.H;
   return (long long)b * p.stride_b + (long long)h * p.stride_h + (long long)c * kT * kD;
@@ -707,7 +716,11 @@ struct ScanParams {
   int reverse;
   float clip;
   unsigned* status;
+  int bh0;                 // first head of this launch
 };
+
+// Descriptor validation shared by every C-ABI entry point (gdn2_api.cu).
+gdn2_status check_desc(const gdn2_desc* d);
 
 cudaError_t launch_fwd_intra(const OpParams& p, bool bf16, int nblocks, cudaStream_t st);
 cudaError_t launch_fwd_out(const OpParams& p, bool bf16, float* o, int nblocks, cudaStream_t st);

@@ -31,7 +31,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanParams sp) 
 
   const int t = threadIdx.x, warp = t >> 5;
   const int tiles = kD / kDV;
-  const int bh = blockIdx.x / tiles, v0 = (blockIdx.x % tiles) * kDV;
+  const int bh = sp.bh0 + (int)(blockIdx.x / tiles), v0 = (blockIdx.x % tiles) * kDV;
   const Mode m = mode_from_enum(sp.mode);
   const uint32_t part = image_part_bytes(m);
   const uint32_t ibytes = image_bytes(m);

@@ -9,10 +9,14 @@ the public operator make_blr_trainable(cfg, scale) with the reference's benchmar
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--dtype fp32|bf16]
 
 N > 1 runs under torchrun, one process per GPU.  The operator shards over batch x heads with no
-communication, so each rank processes its own B4 H6 L2048 shard (weak scaling); time is the max
-over ranks of the device time of the timed region; value = all ranks' tokens / that time.
-Rank 0 prints one JSON line.  `--impl reference` times the CPU oracle (a restatement of the
-reference's pure-JAX path; JAX is not available) on the host cores instead.
+communication (every head is an independent recurrence): the B*H = 24 heads of the one B4 H6 L2048
+problem are split over the ranks ("1 GPU then B x H sharded over 2/4/8"), each
+rank copies in only its heads' inputs and copies out only their results (strong scaling); time is
+the max over ranks of the device time of the timed region; value = the problem's B*L tokens / that
+time.  The line also carries the weak-scaling figure (every rank running a whole B4 H6 L2048
+problem of its own) as the extra field `weak`.  Rank 0 prints one JSON line.  `--impl reference`
+times the CPU oracle (a restatement of the reference's pure-JAX path; JAX is not available) on
+the host cores instead.
 """
 from __future__ import annotations
 
@@ -41,12 +45,12 @@ CFG_KW = dict(bt=128, bc=64, score_bs=128, bs2=64, mb=8, wy_eps=0.0,
               dot_mode="highest", solve_dot_mode="bf16x3", b3_dot_mode="bf16x3")
 
 
-def op_launches(nb, nl, cfg):
-    """This library's kernel launches in one fwd+bwd operator call: per batch group (one launch
-    sequence per stream) and sequence segment, fwd_intra (wide chunks included), the forward scan,
-    fwd_out, bwd_pre, the backward scan, bwd_intra and its wide-channel launch."""
-    import atomic_gdn2.pipeline as _pipe
-    return 7 * len(_pipe._batch_groups(nb)) * math.ceil((nl // T) / cfg.max_chunks_per_call)
+def op_launches(nbh, nl, cfg):
+    """This library's kernel launches in one fwd+bwd operator call over nbh heads: per batch group
+    (one launch sequence per side stream) and segment group, fwd_intra (wide chunks included), the
+    forward scan, fwd_out, bwd_pre, the backward scan, bwd_intra and its wide-channel launch."""
+    from atomic_gdn2 import _lib
+    return 7 * min(_lib.batch_groups(), nbh) * math.ceil((nl // T) / cfg.max_chunks_per_call)
 
 
 def parse():
@@ -84,7 +88,7 @@ def make_inputs(seed, device, dtype, shape=(B, H, L)):
 
 # --------------------------------------------------------------------------------------
 # roofline bookkeeping: per chunk-head algorithmic FLOPs / compulsory HBM bytes per kernel
-# (the split of the reference algorithm's GEMM list and compulsory traffic)
+# (the split of the reference algorithm's GEMM list and compulsory traffic over the kernels)
 # --------------------------------------------------------------------------------------
 # Tensor-core cost of one algorithmic FLOP in a precision mode, in bf16-MMA equivalents: "highest"
 # is three tf32 passes (tf32 MMAs run at half the bf16 rate), "bf16x3" three bf16 passes.
@@ -114,11 +118,14 @@ def kernel_work(s_in, nc, modes):
 
 
 def peaks():
+    """(HBM GB/s, bf16 dense TFLOP/s burst, bf16 dense TFLOP/s sustained, source).  The per-kernel
+    times bench.py reports come from a few isolated steps, so the burst figure is their peak."""
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         j = json.loads(p.read_text())
-        return float(j["hbm_gbs"]), float(j.get("bf16_tflops_sustained", j["bf16_tflops"])), "measured"
-    return 6650.0, 1400.0, "fallback"
+        burst = float(j["bf16_tflops"])
+        return float(j["hbm_gbs"]), burst, float(j.get("bf16_tflops_sustained", burst)), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
 
 
 def ncu_traffic():
@@ -214,37 +221,50 @@ class Clocks:
 # --------------------------------------------------------------------------------------
 # CPU baseline (oracle restatement of the reference's pure-JAX path, all host threads)
 # --------------------------------------------------------------------------------------
-def cpu_sample_tokens_per_s(reps, warmup):
+def cpu_head_seconds(reps, warmup, budget_s=None):
+    """Median seconds of one fwd+bwd of ONE head (B1 H1 L2048 D128, fp32) of the benchmark problem
+    through the CPU oracle with every host thread.  Heads are independent recurrences, so the
+    B4 H6 problem's CPU time is B*H = 24 times this.  With budget_s, reps grow (up to 30) to fill
+    about that many seconds.  Returns (seconds, reps, threads)."""
     from oracle import gdn2_oracle as O  # test infrastructure: used here only as the CPU baseline
     torch.set_num_threads(os.cpu_count() or 1)
     (q, k, v, w, b, g), h0 = O.bench_inputs(1, 1, L, D, 0, dtype=torch.float32)
     ocfg = O.OracleCfg(bt=128, score_bs=128, mb=8, wy_eps=0.0)
+    run = lambda: O.loss_and_grads(q, k, v, w, b, g, D ** -0.5, h0, ocfg)
     for _ in range(warmup):
-        O.loss_and_grads(q, k, v, w, b, g, D ** -0.5, h0, ocfg)
+        run()
     ts = []
-    for _ in range(reps):
+    while len(ts) < reps or (budget_s and sum(ts) < budget_s and len(ts) < 30):
         t0 = time.perf_counter()
-        O.loss_and_grads(q, k, v, w, b, g, D ** -0.5, h0, ocfg)
+        run()
         ts.append(time.perf_counter() - t0)
-    return L / statistics.median(ts), torch.get_num_threads()
+    return statistics.median(ts), len(ts), torch.get_num_threads()
 
 
-CPU_SAMPLE = "B1 H1 L2048 D128 (one of the 24 heads), fp32, fwd+bwd of sum(o^2)+sum(h_final^2), median of reps"
+CPU_SAMPLE = ("one head (B1 H1 L2048 D128) of the B4 H6 problem per timed call, fp32, fwd+bwd of "
+              "sum(o^2)+sum(h_final^2); the problem's time is 24 x the median (heads are independent)")
 
 
 def run_reference(args):
+    """The reference arm: the reference's CPU path (its pure-JAX chunked-WY forward + autograd
+    gradients, restated in PyTorch because JAX is absent) on every host core.  Each timed step is
+    one head of the B4 H6 L2048 problem; `value` is the whole problem's tokens per second
+    (B*L tokens / (24 x the per-head time)); ms_per_step is the time of the timed step itself."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     reps = max(1, args.steps)
-    val, cores = cpu_sample_tokens_per_s(reps, max(1, min(args.warmup, 2)))
+    t_head, n, cores = cpu_head_seconds(reps, max(1, min(args.warmup, 2)))
+    nbh = B * H
+    val = B * L / (nbh * t_head)
     line = {
-        "metric": METRIC, "value": val, "unit": "tokens/s", "n_gpus": args.gpus, "steps": reps,
-        "warmup": args.warmup, "ms_per_step": B * L / val * 1e3, "higher_is_better": True, "scaling": "weak",
+        "metric": METRIC, "value": val, "unit": "tokens/s", "n_gpus": args.gpus, "steps": n,
+        "warmup": args.warmup, "ms_per_step": t_head * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": val / PUBLISHED_TOKS, "dtype": "f32", "data": "synthetic",
         "impl": "reference",
-        "config": {"workload": "B4 H6 L2048 D128 fwd+bwd (sampled as one head)", "global_batch": B,
-                   "seq_len": L, "parallelism": "cpu"},
+        "config": {"workload": "B4 H6 L2048 D128 fwd+bwd, timed one head per step", "global_batch": B,
+                   "seq_len": L, "heads": H, "head_dim": D, "parallelism": "cpu"},
+        "sample_scale": nbh, "problem_ms": nbh * t_head * 1e3,
         "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": CPU_SAMPLE},
         "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "reference is JAX/Pallas (TPU); JAX is not installed here, so the reference's pure-JAX "
@@ -256,9 +276,33 @@ def run_reference(args):
 # --------------------------------------------------------------------------------------
 # our arm
 # --------------------------------------------------------------------------------------
+def _time_graph(step, xs_base, dev, warmup, steps, flush=None):
+    """Capture step(leaf inputs) once into a CUDA graph on a side stream (leaf tensors and warm-up
+    live on the capture stream, so autograd's per-stream bookkeeping stays inside the capture).
+    Returns (graph, captured leaf inputs) or (None, None) when capture is unavailable."""
+    try:
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            xs_g = [t.detach().clone().requires_grad_(True) for t in xs_base]
+            for _ in range(2):
+                step(xs_g)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=side):
+                step(xs_g)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        for _ in range(warmup):
+            graph.replay()
+        return graph, xs_g
+    except Exception as exc:  # pragma: no cover - reported; the eager measurement stands
+        print(f"bench: CUDA graph capture unavailable ({exc}); reporting the eager timing", file=sys.stderr)
+        return None, None
+
+
 def run_ours(args):
     import atomic_gdn2
     from atomic_gdn2 import _lib, make_blr_trainable, make_cfg
+    from atomic_gdn2.sharding import bh_range, shard_heads
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -290,7 +334,16 @@ def run_ours(args):
     if args.dtype == "bf16":
         cfg = cfg.with_(dot_mode="default", solve_dot_mode="default", b3_dot_mode="default")
     fn = make_blr_trainable(cfg, D ** -0.5)
-    xs_base, h0 = make_inputs(1234 + rank, dev, dtype)
+    # the one B4 H6 L2048 problem (same seed on every rank); this rank's heads as (1, n_local, L, D)
+    xs_all, h0_all = make_inputs(1234, dev, dtype)
+    if world > 1:
+        xs_base = [shard_heads(t, rank, world).contiguous() for t in xs_all]
+        h0 = shard_heads(h0_all, rank, world).contiguous()
+    else:
+        xs_base, h0 = xs_all, h0_all
+    hs, he = bh_range(B, H, rank, world)
+    nbh_local = he - hs
+    del xs_all, h0_all
     xs = [t.requires_grad_(True) for t in xs_base]
 
     def step(inputs):
@@ -306,7 +359,9 @@ def run_ours(args):
 
     for _ in range(args.warmup):
         step(xs)
-    # eager timing (every launch issued by Python each step)
+    # eager timing (every launch issued by the host each step; device status checks at their
+    # default, asynchronous setting, as a drop-in caller gets them)
+    atomic_gdn2.set_checks("async")
     barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -315,28 +370,11 @@ def run_ours(args):
         loss, grads = step(xs)
     e1.record()
     torch.cuda.synchronize()
+    atomic_gdn2.set_checks(False)
     eager_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
     # headline: the same step captured once into a CUDA graph and replayed (the analogue of the
     # reference's jitted XLA program: no per-launch host work inside the timed region)
-    # (leaf tensors and warm-up live on the capture stream, so that autograd's per-stream
-    # bookkeeping stays inside the capture)
-    graph = None
-    try:
-        side = torch.cuda.Stream(device=dev)
-        side.wait_stream(torch.cuda.current_stream(dev))
-        with torch.cuda.stream(side):
-            xs_g = [t.detach().clone().requires_grad_(True) for t in xs_base]
-            for _ in range(2):
-                step(xs_g)
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph, stream=side):
-                g_loss, g_grads = step(xs_g)
-        torch.cuda.current_stream(dev).wait_stream(side)
-        for _ in range(args.warmup):
-            graph.replay()
-    except Exception as exc:  # pragma: no cover - reported; the eager measurement stands
-        graph = None
-        print(f"bench: CUDA graph capture unavailable ({exc}); reporting the eager timing", file=sys.stderr)
+    graph, xs_g = _time_graph(step, xs_base, dev, args.warmup, args.steps)
     clocks = Clocks(local)
     clocks.start()
     barrier()
@@ -354,17 +392,71 @@ def run_ours(args):
     barrier()
     clk = clocks.stop()
     ms = max_over_ranks(ms_local)
-    status = atomic_gdn2.last_status()
-    tokens = world * B * L
-    value = tokens / (ms / 1e3)
+    value = B * L / (ms / 1e3)
 
-    # per-kernel device time (CUDA events on the launching stream, inside the library), with the
-    # whole batch as one launch sequence: every launch then covers all B*H*NC chunk-heads, the
-    # units the roofline's algorithmic work counts (the timed step above overlaps batch groups
-    # on separate streams; their launches cover part of the batch and share the GPU)
-    import atomic_gdn2.pipeline as _pipe
-    nstreams = _pipe._nstreams
-    _pipe._nstreams = 1
+    # the reference's benchmark protocol (benchmarks/honest_gdn2.py:99-111): 3 seeds x 3 rounds x
+    # (2 warm-up + 4 timed calls), median per round, median per seed, mean +- SD over seeds; each
+    # timed call is one graph replay of the step on that seed's inputs, max over ranks
+    protocol = None
+    if graph is not None:
+        per_seed = []
+        for seed in (0, 1, 2):
+            xa, _ = make_inputs(seed, dev, dtype)
+            with torch.no_grad():
+                for dst, src in zip(xs_g, xa):
+                    dst.copy_(shard_heads(src, rank, world)[0].reshape(dst.shape) if world > 1 else src)
+            del xa
+            rounds = []
+            for _ in range(3):
+                for _ in range(2):
+                    graph.replay()
+                ts = []
+                for _ in range(4):
+                    a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    barrier()
+                    a.record()
+                    graph.replay()
+                    b_.record()
+                    torch.cuda.synchronize()
+                    ts.append(max_over_ranks(a.elapsed_time(b_)))
+                rounds.append(statistics.median(ts))
+            per_seed.append(statistics.median(rounds))
+        mean = statistics.mean(per_seed)
+        protocol = {"seeds": 3, "rounds": 3, "warmup_calls": 2, "timed_calls": 4,
+                    "ms_per_seed": [round(x, 4) for x in per_seed], "ms_mean": mean,
+                    "ms_sd": statistics.stdev(per_seed), "tokens_per_s": B * L / (mean / 1e3)}
+
+    # weak-scaling figure (extra field): every rank runs a whole B4 H6 L2048 problem of its own
+    weak = None
+    if world > 1:
+        xw, _ = make_inputs(4321 + rank, dev, dtype)
+        with torch.no_grad():
+            h0w = torch.randn(B, H, D, D, device=dev) * 0.01
+
+        def step_w(inputs):
+            o, hf = fn(*inputs, h0w)
+            return torch.autograd.grad((o * o).sum() + (hf * hf).sum(), inputs)
+
+        gw, _ = _time_graph(step_w, xw, dev, args.warmup, args.steps)
+        if gw is not None:
+            barrier()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.steps):
+                gw.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            ms_w = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+            weak = {"value": world * B * L / (ms_w / 1e3), "unit": "tokens/s", "ms_per_step": ms_w,
+                    "workload": "B4 H6 L2048 D128 per GPU (every rank its own problem)"}
+            del gw
+        del xw
+
+    # per-kernel device time (CUDA events on the launching stream, inside the library) with this
+    # rank's heads as one launch sequence (one batch group), so that every launch covers all of the
+    # rank's chunk-heads, the units the roofline's algorithmic work counts
+    groups = _lib.set_batch_groups(1)
     _lib.profile_enable(True)
     nprof = 3
     for _ in range(nprof):
@@ -372,27 +464,40 @@ def run_ours(args):
     torch.cuda.synchronize()
     prof = _lib.profile_collect()
     _lib.profile_enable(False)
-    _pipe._nstreams = nstreams
+    _lib.set_batch_groups(groups)
 
-    # end to end through the public API with host buffers: every step copies its inputs from
-    # pinned host memory and reads its loss back.  The copy of step i+1's inputs runs on a copy
-    # stream while step i computes (two device input buffers, events order reuse), as a serving
-    # or training input pipeline would; the compute stream waits for each copy.
-    # The pinned buffers are allocated and filled from the CPUs local to the GPU (NVML's affinity
-    # mask), as an input pipeline placed on the GPU's NUMA node would; the process's affinity is
-    # restored after the end-to-end timing (the CPU baseline below uses every core).
+    # end to end through the public API with host buffers: every step copies this rank's inputs
+    # from pinned host memory, and copies its results (o, h_final and the six gradients) back to
+    # pinned host memory, and reads its loss.  The copy of step i+1's inputs runs on a copy stream
+    # while step i computes (two device input buffers, events order reuse); step i's results go
+    # out on a third stream while step i+1 computes; step i's loss is read once step i+1 has been
+    # issued.  The pinned buffers are allocated and filled from the CPUs local to the GPU (NVML's
+    # affinity mask), as an input pipeline placed on the GPU's NUMA node would; the process's
+    # affinity is restored afterwards (the CPU baseline below uses every core).
     saved_affinity = os.sched_getaffinity(0)
     local_cpus = gpu_local_cpus(dev)
     if local_cpus:
         os.sched_setaffinity(0, local_cpus)
     host = [t.detach().cpu().pin_memory() for t in xs_base]
     h2d = sum(t.numel() * t.element_size() for t in host)
+    out_shapes = [((1 if world > 1 else B), (nbh_local if world > 1 else H), L, D, torch.float32),
+                  ((1 if world > 1 else B), (nbh_local if world > 1 else H), D, D, torch.float32)]
+    out_shapes += [tuple(t.shape) + (t.dtype,) for t in xs_base]
+    host_out = [[torch.empty(sh[:-1], dtype=sh[-1]).pin_memory() for sh in out_shapes] for _ in range(2)]
+    d2h = sum(t.numel() * t.element_size() for t in host_out[0]) + 4
     e2e_steps = max(3, min(args.steps, 30))
     cs = torch.cuda.Stream(device=dev)
+    os_ = torch.cuda.Stream(device=dev)
     bufs = [[torch.empty_like(t).requires_grad_(True) for t in xs_base] for _ in range(2)]
     ready = [torch.cuda.Event() for _ in range(2)]
     free = [torch.cuda.Event() for _ in range(2)]
     cur = torch.cuda.current_stream(dev)
+
+    def step_out(inputs):
+        o, hf = fn(*inputs, h0)
+        loss = (o * o).sum() + (hf * hf).sum()
+        grads = torch.autograd.grad(loss, inputs)
+        return loss, [o.detach(), hf.detach(), *grads]
 
     def issue_copy(i, after=None):
         bi = i % 2
@@ -407,15 +512,27 @@ def run_ours(args):
 
     def run_e2e(n, start_event=None):
         issue_copy(0, start_event)
+        pending = None
         lv = None
         for i in range(n):
             if i + 1 < n:
                 issue_copy(i + 1)
             bi = i % 2
             cur.wait_event(ready[bi])
-            loss, _ = step(bufs[bi])
+            loss, outs = step_out(bufs[bi])
             free[bi].record(cur)
-            lv = loss.item()
+            done = torch.cuda.Event()
+            done.record(cur)
+            with torch.cuda.stream(os_):
+                os_.wait_event(done)
+                for dst, src in zip(host_out[bi], outs):
+                    dst.copy_(src, non_blocking=True)
+                    src.record_stream(os_)
+            if pending is not None:
+                lv = pending.item()
+            pending = loss
+        lv = pending.item()
+        cur.wait_stream(os_)
         return lv
 
     run_e2e(2)
@@ -428,72 +545,92 @@ def run_ours(args):
     torch.cuda.synchronize()
     barrier()
     e2e_ms = max_over_ranks(f0.elapsed_time(f1) / e2e_steps)
-    e2e_val = tokens / (e2e_ms / 1e3)
+    e2e_val = B * L / (e2e_ms / 1e3)
     os.sched_setaffinity(0, saved_affinity)
+    status = atomic_gdn2.last_status()
+    status = int(max_over_ranks(float(status)))
 
     if rank == 0:
-        hbm, tflops, peak_kind = peaks()
+        hbm, tf_burst, tf_sust, peak_kind = peaks()
         modes = {k: cfg.__dict__[k] for k in ("dot_mode", "solve_dot_mode", "b3_dot_mode")}
         work = kernel_work(s_in, L // T, modes)
-        nch = B * H * (L // T)
-        traffic = ncu_traffic() if dtype == torch.float32 else {}
+        nch = nbh_local * (L // T)
+        traffic = ncu_traffic() if (dtype == torch.float32 and world == 1) else {}
         kern = {}
         for name, (tot_ms, cnt) in prof.items():
             if cnt == 0:
                 continue
             per = tot_ms / cnt
             f, f_eff, by = work[name]
-            t_f = f_eff * nch / (tflops * 1e12)
-            t_b = by * nch / (hbm * 1e9)
-            kern[name] = {"ms_per_launch": per, "share": tot_ms, "flops": f * nch, "flops_eff": f_eff * nch,
-                          "bytes": by * nch, "t_roof_ms": max(t_f, t_b) * 1e3,
+            t_f = f * nch / (tf_burst * 1e12)          # algorithmic FLOPs at the measured bf16 peak
+            t_b = by * nch / (hbm * 1e9)               # compulsory bytes at the measured HBM copy rate
+            t_mode = f_eff * nch / (tf_burst * 1e12)   # estimate: FLOPs at the modes' MMA cost
+            kern[name] = {"ms_per_launch": per, "share": tot_ms, "flops": f * nch, "bytes": by * nch,
+                          "t_roof_ms": max(t_f, t_b) * 1e3, "t_mode_ms": max(t_mode, t_b) * 1e3,
                           "bound": "tensor" if t_f >= t_b else "hbm"}
         tot = sum(k["share"] for k in kern.values()) or 1.0
         for k in kern.values():
             k["share"] = k["share"] / tot
         dom = max(kern, key=lambda n: kern[n]["share"])
         kd = kern[dom]
-        if kd["bound"] == "tensor":
-            # algorithmic TFLOP/s against the mode's effective peak (measured bf16 peak / mode cost)
-            achieved = kd["flops"] / (kd["ms_per_launch"] / 1e3) / 1e12
-            peak, unit = tflops * kd["flops"] / kd["flops_eff"], "TFLOP/s"
-        else:
-            achieved, peak, unit = kd["bytes"] / (kd["ms_per_launch"] / 1e3) / 1e9, hbm, "GB/s"
-        # whole-step roofline: the kernels' roofline times over the measured step time
+        sec = kd["ms_per_launch"] / 1e3
+        tensor = {"achieved": kd["flops"] / sec / 1e12, "peak": tf_burst, "unit": "TFLOP/s"}
+        tensor["frac"] = tensor["achieved"] / tensor["peak"]
+        mem = {"achieved": kd["bytes"] / sec / 1e9, "peak": hbm, "unit": "GB/s"}
+        mem["frac"] = mem["achieved"] / mem["peak"]
+        main_ = tensor if kd["bound"] == "tensor" else mem
         t_step_roof = sum(k["t_roof_ms"] for k in kern.values())
+        t_step_mode = sum(k["t_mode_ms"] for k in kern.values())
         cpu = None
         if world == 1:
-            val_cpu, cores = cpu_sample_tokens_per_s(3, 1)
-            cpu = {"value": val_cpu, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": CPU_SAMPLE}
+            t_head, n_cpu, cores = cpu_head_seconds(3, 1, budget_s=10.0)
+            cpu = {"value": B * L / (B * H * t_head), "unit": "tokens/s", "cores": cores, "kind": "port",
+                   "sample": CPU_SAMPLE + f" ({n_cpu} timed calls)"}
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": value / PUBLISHED_TOKS,
             "timing": "CUDA-graph replay of the whole step" if graph is not None else "eager launches",
             "eager_ms_per_step": eager_ms,
             "dtype": "f32" if dtype == torch.float32 else "bf16", "data": "synthetic",
-            "config": {"workload": "B4 H6 L2048 D128 per GPU, fwd+bwd of sum(o^2)+sum(h_final^2) w.r.t. q,k,v,w,b,g",
-                       "global_batch": B * world, "seq_len": L, "heads": H, "head_dim": D,
-                       "parallelism": f"bh-shard x{world}",
-                       "modes": {k: cfg.__dict__[k] for k in ("dot_mode", "solve_dot_mode", "b3_dot_mode")},
-                       "l2": "inputs (6 x 25 MB) and residuals (~250 MB) exceed the 126 MB L2"},
-            "roofline": {"kernel": dom, "bound": kd["bound"], "achieved": achieved, "peak": peak, "unit": unit,
-                         "frac": achieved / peak, "traffic": traffic.get(dom), "peak_source": peak_kind,
-                         "peak_note": "tensor peak = measured sustained bf16 dense peak / the precision mode's "
-                                      "MMA cost per FLOP (3 x tf32 = 6, 3 x bf16 = 3, bf16 = 1)",
-                         "step_frac": t_step_roof / ms},
+            "config": {"workload": "B4 H6 L2048 D128 fwd+bwd of sum(o^2)+sum(h_final^2) w.r.t. q,k,v,w,b,g"
+                                   + (f", its 24 heads sharded over {world} GPUs" if world > 1 else ""),
+                       "global_batch": B, "seq_len": L, "heads": H, "head_dim": D,
+                       "parallelism": f"bh-shard x{world}" if world > 1 else "1 GPU",
+                       "heads_per_gpu": nbh_local, "batch_groups": _lib.batch_groups(),
+                       "modes": modes,
+                       "l2": "inputs (6 x 25 MB), residuals (127 MB) and workspaces exceed the 126 MB L2"},
+            "roofline": {"kernel": dom, "bound": kd["bound"], "achieved": main_["achieved"], "peak": main_["peak"],
+                         "unit": main_["unit"], "frac": main_["frac"], "traffic": traffic.get(dom),
+                         "algorithmic_bytes": kd["bytes"], "algorithmic_flops": kd["flops"],
+                         "peak_source": f"{peak_kind} (bf16 dense burst; HBM copy)",
+                         "tensor": tensor, "hbm": mem,
+                         "bound_note": "bound = the larger of algorithmic FLOPs at the measured bf16 dense peak and "
+                                       "compulsory bytes at the measured HBM rate",
+                         "step_frac": t_step_roof / ms,
+                         "mode_adjusted_estimate": {
+                             "note": "unmeasured estimate: each FLOP at its precision mode's MMA cost in bf16-MMA "
+                                     "equivalents (3 x tf32 = 6, 3 x bf16 = 3, bf16 = 1)",
+                             "kernel_frac": kd["t_mode_ms"] / kd["ms_per_launch"],
+                             "step_frac": t_step_mode / ms}},
             "kernels": {n: {"ms": round(v["ms_per_launch"], 4), "share": round(v["share"], 3),
-                            "bound": v["bound"], "roof_ms": round(v["t_roof_ms"], 4)} for n, v in kern.items()},
+                            "bound": v["bound"], "roof_ms": round(v["t_roof_ms"], 4),
+                            "frac": round(v["t_roof_ms"] / v["ms_per_launch"], 4)} for n, v in kern.items()},
+            "protocol": protocol,
+            "weak": weak,
             "cpu_baseline": cpu,
-            "e2e": {"value": e2e_val, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
-                    "ms_per_step": e2e_ms, "pipeline": "next step's H2D overlapped with this step's compute",
+            "e2e": {"value": e2e_val, "unit": "tokens/s", "h2d_bytes_per_step": h2d * world,
+                    "d2h_bytes_per_step": d2h * world, "ms_per_step": e2e_ms,
+                    "copies": "inputs q,k,v,w,b,g H2D; o, h_final, dq..dg D2H; loss read per step",
+                    "pipeline": "next step's H2D and previous step's D2H overlapped with this step's compute",
                     "host_buffers": ("pinned, on the GPU's local CPUs (NVML affinity, %d CPUs)" % len(local_cpus))
                     if local_cpus else "pinned"},
-            "gpu_launches": op_launches(B, L, cfg) * args.steps,
+            "gpu_launches": op_launches(nbh_local, L, cfg) * args.steps,
             "clocks": clk,
             "device_status": status,
         }
         print(json.dumps(line), flush=True)
+    del graph
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -637,7 +774,7 @@ def run_lm(args):
 
     atomic_gdn2.set_checks(True)
     step(tokens())
-    atomic_gdn2.set_checks(False)
+    atomic_gdn2.set_checks("async")    # the default a drop-in caller gets: no host synchronisation
     steps, warmup = max(1, min(args.steps, 20)), max(3, args.warmup)
     batches = [tokens() for _ in range(steps)]
     for _ in range(warmup):
@@ -670,15 +807,13 @@ def run_lm(args):
     # operator kernels inside one step, with each operator call's batch as one launch sequence so
     # that launches do not overlap and their durations add up (the timed steps overlap the batch
     # groups on their streams)
-    import atomic_gdn2.pipeline as _pipe
-    nstreams = _pipe._nstreams
-    _pipe._nstreams = 1
+    groups = _lib.set_batch_groups(1)
     _lib.profile_enable(True)
     step(batches[0])
     torch.cuda.synchronize()
     prof = _lib.profile_collect()
     _lib.profile_enable(False)
-    _pipe._nstreams = nstreams
+    _lib.set_batch_groups(groups)
     # end to end: tokens from pinned host memory every step, loss read back every step
     host = [b.cpu().pin_memory() for b in batches]
     torch.cuda.synchronize()
@@ -717,7 +852,7 @@ def run_lm(args):
             "operator_kernels_ms_per_step": op_ms,
             "operator_share": sum(op_ms.values()) / ms,  # of the timed (overlapped) step: an upper bound
             "e2e": {"value": e2e_ms, "unit": "ms", "h2d_bytes_per_step": LM_B * LM_L * 8, "d2h_bytes_per_step": 4},
-            "gpu_launches": (op_launches(LM_B, LM_L, cfg) + 2) * len(model.layers) * steps,
+            "gpu_launches": (op_launches(LM_B * mc["n_heads"], LM_L, cfg) + 2) * len(model.layers) * steps,
             "final_loss": final_loss,
             "published_other_model_ms": LM_PUBLISHED_MS_OTHER_MODEL,
             "clocks": clk, "device_status": status,

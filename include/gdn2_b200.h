@@ -77,9 +77,14 @@ typedef struct gdn2_desc {
   int32_t in_dtype;          /* gdn2_dtype of q..g and of the six gradients */
 } gdn2_desc;
 
-/* Bytes of the residual buffer gdn2_fwd fills and gdn2_bwd reads for one call
- * (forward intermediates: scores, WY inverse, per-chunk states, ...). */
+/* Bytes of the residual buffer gdn2_fwd fills and gdn2_bwd reads for one call: the forward
+ * intermediates the backward needs (scores Aqk, WY inverse A, wp, the state entering every chunk,
+ * v_new).  The reference keeps gc, Aqk, A, h_pre_all, v_new_all (pipeline.py:25-26). */
 size_t gdn2_residual_bytes(const gdn2_desc* desc);
+
+/* Bytes of scratch gdn2_fwd needs beyond the residual buffer, dead once the call's work has run on
+ * the stream (u = A (w v), the forward scan's state-transition images and additive terms). */
+size_t gdn2_fwd_workspace_bytes(const gdn2_desc* desc);
 
 /* Bytes of scratch gdn2_bwd needs beyond the residual buffer. */
 size_t gdn2_bwd_workspace_bytes(const gdn2_desc* desc);
@@ -90,12 +95,13 @@ size_t gdn2_bwd_workspace_bytes(const gdn2_desc* desc);
  *   h0        (B,H,D,D) fp32 initial state, or NULL for zeros (pipeline.py:57)
  *   o         (B,H,L,D) fp32 output
  *   h_final   (B,H,D,D) fp32 final state
- *   residual  gdn2_residual_bytes(desc) bytes, 256-byte aligned
- *   dev_status device uint32 the kernels OR status bits into (caller zeroes it)
- *   stream    cudaStream_t */
+ *   residual  gdn2_residual_bytes(desc) bytes, 256-byte aligned (kept for gdn2_bwd)
+ *   workspace gdn2_fwd_workspace_bytes(desc) bytes, 256-byte aligned (free after the call's work)
+ *   dev_status device uint32 the kernels OR status bits into (never cleared by the library)
+ *   stream    cudaStream_t; the work is ordered on it (see gdn2_set_batch_groups) */
 gdn2_status gdn2_fwd(const gdn2_desc* desc, const void* q, const void* k, const void* v, const void* w,
                      const void* b, const void* g, const float* h0, float* o, float* h_final, void* residual,
-                     uint32_t* dev_status, void* stream);
+                     void* workspace, uint32_t* dev_status, void* stream);
 
 /* Backward of one segment.  Replaces core_bwd (pipeline.py:38-47 ->
  * backward_mega, bwd/mega.py:61-79).
@@ -109,6 +115,16 @@ gdn2_status gdn2_bwd(const gdn2_desc* desc, const void* q, const void* k, const 
                      const void* b, const void* g, const void* residual, const float* d_o, const float* d_hfinal,
                      void* dq, void* dk, void* dv, void* dw, void* db, void* dg, float* dh0, void* workspace,
                      uint32_t* dev_status, void* stream);
+
+/* Batch groups (no counterpart in the reference; an execution setting, not part of the
+ * arithmetic).  gdn2_fwd / gdn2_bwd split a call's B*H heads into up to n contiguous groups whose
+ * launch sequences run on side streams the library owns, forked from the caller's stream by an
+ * event and joined back to it before the call returns (capturable into a CUDA graph; the streams
+ * are created by the first multi-group call on a device, which must not be under capture -- a call
+ * under capture before that runs as one group).  Results do not depend on n.  n is clamped to
+ * [1, 8]; the initial value is the environment's GDN2_STREAMS, else 4.  Returns the previous value. */
+int32_t gdn2_set_batch_groups(int32_t n);
+int32_t gdn2_get_batch_groups(void);
 
 /* Human-readable name of a status code (static string). */
 const char* gdn2_status_string(gdn2_status status);
@@ -146,16 +162,19 @@ gdn2_status gdn2_selftest_wait_timeout(uint32_t* dev_status, int64_t limit_cycle
                                        void* stream);
 
 /* Allocation-free forward (no counterpart in the reference).  Same arguments and results as
- * gdn2_fwd minus the residual buffer: the scratch lives in a fixed 64 MiB device array inside the
- * library, so the call performs no device allocation.  It is meant for callers that cannot
+ * gdn2_fwd minus the residual and workspace buffers: both live in a fixed 64 MiB device array
+ * inside the library, so the call performs no device allocation.  It is meant for callers that cannot
  * allocate at the point where they run the operator, such as runtime plugin / custom-call hooks
  * whose device memory is owned and planned by the host framework's allocator, and which receive
  * only a stream plus their input and output pointers.
- *   Limit: gdn2_residual_bytes(desc) must be <= 64 MiB (about 96 chunk-heads of 128 tokens in
+ *   Limit: gdn2_residual_bytes(desc) rounded up to 256 bytes plus gdn2_fwd_workspace_bytes(desc)
+ *   must be <= 64 MiB (about 96 chunk-heads of 128 tokens in
  *   the default modes, e.g. B=1, H=6, L=2048); larger problems are rejected with
- *   GDN2_ERR_INVALID_ARGUMENT before any launch.
+ *   GDN2_ERR_INVALID_ARGUMENT before any launch; a descriptor gdn2_fwd rejects gets the same
+ *   status here (GDN2_ERR_UNSUPPORTED for a chunk length or head size this build lacks).
  *   The first call on each device looks up the array's device address (cudaGetSymbolAddress);
- *   make that first call before any stream capture.
+ *   make that first call before any stream capture.  The address is kept for the life of the
+ *   process: do not use this entry point across a cudaDeviceReset of that device.
  *   All calls on a device share the one array: calls that overlap on the GPU (different streams
  *   without ordering) race on it.  No state carries from one call to the next.
  *   Forward only: there is no residual to hand to gdn2_bwd. */

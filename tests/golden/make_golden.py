@@ -16,7 +16,7 @@ and the derivative of value w.r.t. theta at theta = 0 (a directional derivative 
 `direction` applied to v).  These Decimal numbers are the golden values; no other stored
 operator outputs exist in the reference (KNOWN_LIMITATIONS.md:59).
 
-Run from the repository root:  python tests/golden/make_golden.py [reference_root]
+Run from the repository root:  python tests/golden/make_golden.py <reference_root>
 """
 from __future__ import annotations
 
@@ -64,4 +64,6 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: python tests/golden/make_golden.py <root of the reference checkout>")
+    main(sys.argv[1])

@@ -78,9 +78,14 @@ def test_residual_sizes_and_validation():
     assert ok > 0 and ok % 256 == 0
     # dvl, Cc, dh states, dAqk, dAkk (fp32) + the transposed transition image (bf16x3: 64 KB per chunk-head)
     assert lib.gdn2_bwd_workspace_bytes(ctypes.byref(_desc())) == 5 * 2 * 2 * 128 * 128 * 4 + 2 * 2 * 65536
-    # fp32 residual scales with the number of chunk-heads
+    # the residual (kept for the backward) at the benchmark shape B4 H6 L2048: Aqk, A, wp, v_new
+    # (64 KB per chunk-head each) and the states entering every chunk plus h_final (64 KB each)
     big = lib.gdn2_residual_bytes(ctypes.byref(_desc(B=4, H=6, L=2048)))
-    assert 180e6 < big < 300e6
+    mat = 128 * 128 * 4
+    assert big == 4 * 384 * mat + 24 * 17 * mat + 384 * 4
+    # the forward workspace (dead after the call): u, Bc and the fp32-mode transition images (hi + lo)
+    fws = lib.gdn2_fwd_workspace_bytes(ctypes.byref(_desc(B=4, H=6, L=2048)))
+    assert fws == 2 * 384 * mat + 384 * 2 * mat
     for bad in (dict(L=200), dict(dot=7), dict(dtype=5), dict(wy_eps=1.5), dict(stride_h=100)):
         assert lib.gdn2_residual_bytes(ctypes.byref(_desc(**bad))) == 0, bad
 
@@ -89,14 +94,16 @@ def test_entry_points_reject_bad_arguments_without_gpu():
     lib = _lib.load()
     null = ctypes.c_void_p(0)
     # invalid descriptor: L not a multiple of bt -> GDN2_ERR_INVALID_ARGUMENT before any launch
-    rc = lib.gdn2_fwd(ctypes.byref(_desc(L=200)), *[null] * 12)
+    rc = lib.gdn2_fwd(ctypes.byref(_desc(L=200)), *[null] * 13)
     assert rc == _lib.ERR_INVALID_ARGUMENT
     # unsupported geometry (D != 128)
-    rc = lib.gdn2_fwd(ctypes.byref(_desc(D=64, stride_h=256 * 64)), *[null] * 12)
+    rc = lib.gdn2_fwd(ctypes.byref(_desc(D=64, stride_h=256 * 64)), *[null] * 13)
     assert rc == _lib.ERR_UNSUPPORTED
     # null pointers with a valid descriptor
-    rc = lib.gdn2_fwd(ctypes.byref(_desc()), *[null] * 12)
+    rc = lib.gdn2_fwd(ctypes.byref(_desc()), *[null] * 13)
     assert rc == _lib.ERR_INVALID_ARGUMENT
+    for bad in (dict(L=200), dict(dot=7)):
+        assert lib.gdn2_fwd_workspace_bytes(ctypes.byref(_desc(**bad))) == 0, bad
     rc = lib.gdn2_bwd(ctypes.byref(_desc()), *[null] * 19)
     assert rc == _lib.ERR_INVALID_ARGUMENT
     # the wait self-test refuses a missing status word and limits outside (0, 8e9] cycles
@@ -159,12 +166,17 @@ def test_segment_groups_cover_the_sequence(monkeypatch):
     lib = _lib.load()
     cfg = make_cfg(max_chunks_per_call=32)
     args = (lib, cfg, 0.1, 1, 6, 128, 6 * 65536 * 128, 65536 * 128, torch.float32, 512)
-    assert pipeline._segment_groups(*args) == [(0, 512)]          # 16 segments, one launch sequence
+
+    def groups():
+        pipeline._plans.clear()
+        return [(sg.a, sg.c) for sg in pipeline._plan(*args)]
+
+    assert groups() == [(0, 512)]          # 16 segments, one launch sequence
     monkeypatch.setattr(pipeline, "_group_bytes", 1)
-    g = pipeline._segment_groups(*args)
-    assert g == [(s, s + 32) for s in range(0, 512, 32)]
+    assert groups() == [(s, s + 32) for s in range(0, 512, 32)]
     one = pipeline._make_desc(cfg, 0.1, 1, 6, 32 * 128, 128, 6 * 65536 * 128, 65536 * 128, torch.float32)
     ws = lib.gdn2_bwd_workspace_bytes(ctypes.byref(one))
     monkeypatch.setattr(pipeline, "_group_bytes", 3 * ws + 1)
-    g = pipeline._segment_groups(*args)
+    g = groups()
+    pipeline._plans.clear()
     assert g[0] == (0, 96) and g[-1][1] == 512 and all(b == c for (_, b), (c, _) in zip(g, g[1:]))

@@ -4,9 +4,11 @@ gdn2_fwd_noalloc exists for callers that cannot allocate device memory where the
 operator (runtime plugin / custom-call hooks whose memory is owned by the framework's
 allocator); it keeps its scratch in a fixed device array inside the library.  This test calls
 both entry points through the C ABI on the same inputs, twice in a row (the second call sees the
-first call's leftovers in the shared scratch), compares o and h_final within the fp32 parity
-tolerance of the other GPU tests (rel-L2 1e-4), and checks that a problem larger than the
-scratch is refused before any launch.  It lives in its own file, collected last.
+first call's leftovers in the shared scratch).  Both run the same kernels on the same inputs with
+the same launch shapes, so o and h_final must agree bit for bit (a tolerance could hide a
+scratch-overlap bug).  It also checks that a problem larger than the scratch is refused before
+any launch with GDN2_ERR_INVALID_ARGUMENT, and that a geometry this build does not implement gets
+the same GDN2_ERR_UNSUPPORTED as from gdn2_fwd.  It lives in its own file, collected last.
 """
 import ctypes
 
@@ -57,9 +59,10 @@ def test_noalloc_forward_matches_regular_forward():
     for call, seed in enumerate((11, 12)):
         xs, h0 = _inputs(B, H, L, seed)
         res = torch.empty(lib.gdn2_residual_bytes(ctypes.byref(desc)), dtype=torch.uint8, device="cuda")
+        fws = torch.empty(lib.gdn2_fwd_workspace_bytes(ctypes.byref(desc)), dtype=torch.uint8, device="cuda")
         o_ref = torch.empty(B, H, L, D, device="cuda")
         hf_ref = torch.empty(B, H, D, D, device="cuda")
-        rc = lib.gdn2_fwd(ctypes.byref(desc), *map(_p, xs), _p(h0), _p(o_ref), _p(hf_ref), _p(res), _p(status),
+        rc = lib.gdn2_fwd(ctypes.byref(desc), *map(_p, xs), _p(h0), _p(o_ref), _p(hf_ref), _p(res), _p(fws), _p(status),
                           stream)
         assert rc == _lib.OK
         o = torch.full((B, H, L, D), float("nan"), device="cuda")
@@ -68,13 +71,22 @@ def test_noalloc_forward_matches_regular_forward():
         assert rc == _lib.OK, f"call {call}: {_lib.status_string(rc)}"
         torch.cuda.synchronize()
         assert int(status.item()) == 0
-        assert _rel(o, o_ref) < 1e-4 and _rel(hf, hf_ref) < 1e-4, call
+        assert torch.equal(o, o_ref) and torch.equal(hf, hf_ref), (call, _rel(o, o_ref), _rel(hf, hf_ref))
 
 
 def test_noalloc_rejects_problems_beyond_its_scratch():
     lib = _lib.load()
-    desc = _desc(4, 6, 2048)      # 384 chunk-heads: needs ~253 MB of scratch
-    assert lib.gdn2_residual_bytes(ctypes.byref(desc)) > (64 << 20)
+    desc = _desc(4, 6, 2048)      # 384 chunk-heads: needs ~230 MB of scratch
+    assert lib.gdn2_residual_bytes(ctypes.byref(desc)) + lib.gdn2_fwd_workspace_bytes(ctypes.byref(desc)) > (64 << 20)
     null = ctypes.c_void_p(0)
     rc = lib.gdn2_fwd_noalloc(ctypes.byref(desc), *[null] * 11)
     assert rc == _lib.ERR_INVALID_ARGUMENT
+
+
+def test_noalloc_reports_unsupported_geometry_like_gdn2_fwd():
+    lib = _lib.load()
+    desc = _desc(1, 1, 256)
+    desc.bt = 64                  # a chunk length the reference accepts but this build does not implement
+    null = ctypes.c_void_p(0)
+    assert lib.gdn2_fwd(ctypes.byref(desc), *[null] * 13) == _lib.ERR_UNSUPPORTED
+    assert lib.gdn2_fwd_noalloc(ctypes.byref(desc), *[null] * 11) == _lib.ERR_UNSUPPORTED
