@@ -142,13 +142,33 @@ def test_segment_grouping_is_exact(monkeypatch):
     from atomic_gdn2 import pipeline
     cfg = make_cfg(max_chunks_per_call=2)
     xs, h0 = O.bench_inputs(1, 2, 1024, D, 5)
+    monkeypatch.setattr(pipeline, "_plans", {})
     grouped = _run_op(cfg, xs, h0)
+    assert len(next(iter(pipeline._plans.values()))) == 1
     monkeypatch.setattr(pipeline, "_group_bytes", 1)      # every group is a single segment
-    assert len(pipeline._segment_groups(pipeline._lib.load(), cfg, 0.1, 1, 2, D, 2 * 1024 * D, 1024 * D,
-                                        torch.float32, 8)) == 4
+    monkeypatch.setattr(pipeline, "_plans", {})
     per_segment = _run_op(cfg, xs, h0)
+    assert len(next(iter(pipeline._plans.values()))) == 4
     for x, y in zip(grouped, per_segment):
         assert torch.equal(x, y)
+
+
+def test_batch_groups_do_not_change_results():
+    """The library's batch groups (heads split over forked side streams) only change the schedule:
+    one, two, three and eight groups give bit-identical o, h_final and gradients."""
+    from atomic_gdn2 import _lib
+    cfg = make_cfg()
+    xs, h0 = O.bench_inputs(2, 3, 384, D, 6)
+    prev = _lib.set_batch_groups(1)
+    try:
+        ref = _run_op(cfg, xs, h0)
+        for g in (2, 3, 8):
+            _lib.set_batch_groups(g)
+            assert _lib.batch_groups() == g
+            got = _run_op(cfg, xs, h0)
+            assert all(torch.equal(x, y) for x, y in zip(ref, got)), g
+    finally:
+        _lib.set_batch_groups(prev)
 
 
 def test_determinism():
