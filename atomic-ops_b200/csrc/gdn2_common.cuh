@@ -144,16 +144,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 // Wait for the phase with the given parity to complete; never spins forever: after `limit` SM
 // cycles the wait gives up, sets the timeout bit of the caller's status word and returns false.
+// Once any wait of the call has given up (the bit is set), later waits give up at once, so that a
+// call whose waits cannot complete ends after one limit instead of one limit per wait.
 __device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, unsigned* status, long long limit) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 1023u) == 0 && (*reinterpret_cast<volatile unsigned*>(status) & kStatusTimeout)) return false;
     if (clock64() - t0 > limit) {
       atomicOr(status, kStatusTimeout);
       return false;
     }
   }
-  return true;
 }
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned* status) {
   return mbar_wait_for(bar, parity, status, kWaitCycles);
