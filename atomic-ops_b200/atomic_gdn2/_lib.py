@@ -61,7 +61,7 @@ def _declare(lib):
     lib.gdn2_get_batch_groups.restype = ctypes.c_int32
     lib.gdn2_get_batch_groups.argtypes = []
     lib.gdn2_bwd.restype = ctypes.c_int
-    lib.gdn2_bwd.argtypes = [ctypes.POINTER(Gdn2Desc)] + [P] * 19
+    lib.gdn2_bwd.argtypes = [ctypes.POINTER(Gdn2Desc)] + [P] * 20
     lib.gdn2_status_string.restype = ctypes.c_char_p
     lib.gdn2_status_string.argtypes = [ctypes.c_int]
     lib.gdn2_selftest_gemm.restype = ctypes.c_int

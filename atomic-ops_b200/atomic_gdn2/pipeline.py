@@ -239,7 +239,7 @@ class _GDN2(torch.autograd.Function):
         el = q.element_size()
         stream = _stream()
         h = h0
-        saved = []
+        saved, finals = [], []
         plan = _plan(lib, cfg, scale, B, H, D, sb, sh, q.dtype, nc)
         for si, sg in enumerate(plan):
             res = torch.empty(sg.res_bytes, dtype=torch.uint8, device=dev)
@@ -252,18 +252,22 @@ class _GDN2(torch.autograd.Function):
                               _ptr(res), _ptr(fws), _ptr(st.word), stream)
             _lib.check(rc, "gdn2_fwd")
             saved.append(res if need_res else None)
+            if not last:
+                finals.append(h_out)      # the segment's final state: read by its backward
             h = h_out
         _after_call(st, "gdn2_fwd")
-        ctx.cfg, ctx.plan, ctx.res = cfg, plan, saved
+        ctx.cfg, ctx.plan, ctx.res, ctx.finals = cfg, plan, saved, finals
         ctx.h0_dtype = None if h0 is None else h0.dtype
-        ctx.save_for_backward(q, k, v, w, b, g)
+        # h_final (an output) is saved so that an in-place change of it before backward is caught
+        ctx.save_for_backward(q, k, v, w, b, g, h_final)
         return o, h_final
 
     @staticmethod
     def backward(ctx, do, dhf):
         lib = _lib.load()
         cfg = ctx.cfg
-        q, k, v, w, b, g = ctx.saved_tensors
+        q, k, v, w, b, g, h_final = ctx.saved_tensors
+        finals = ctx.finals + [h_final]
         B, H, L, D = q.shape
         dev = q.device
         if any(res is None for res in ctx.res):
@@ -292,8 +296,8 @@ class _GDN2(torch.autograd.Function):
             dh0 = dh0_all if si == 0 else torch.empty((B, H, D, D), dtype=torch.float32, device=dev)
             ins = [ctypes.c_void_p(t.data_ptr() + off * el) for t in (q, k, v, w, b, g)]
             outs = [ctypes.c_void_p(t.data_ptr() + off * el) for t in grads]
-            rc = lib.gdn2_bwd(sg.ref, *ins, _ptr(res), ctypes.c_void_p(do_s.data_ptr() + off * 4), _ptr(dh), *outs,
-                              _ptr(dh0), _ptr(ws), _ptr(st.word), stream)
+            rc = lib.gdn2_bwd(sg.ref, *ins, _ptr(res), _ptr(finals[si]), ctypes.c_void_p(do_s.data_ptr() + off * 4),
+                              _ptr(dh), *outs, _ptr(dh0), _ptr(ws), _ptr(st.word), stream)
             _lib.check(rc, "gdn2_bwd")
             dh = dh0
         _after_call(st, "gdn2_bwd")

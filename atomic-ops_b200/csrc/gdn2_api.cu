@@ -248,8 +248,7 @@ extern "C" gdn2_status gdn2_fwd(const gdn2_desc* d, const void* q, const void* k
   sb.add = reinterpret_cast<const float*>(static_cast<uint8_t*>(workspace) + base.rl.bc);
   sb.state_in = h0;
   sb.states = reinterpret_cast<float*>(base.res + base.rl.hs);
-  sb.states_per_head = NC + 1;
-  sb.store_final_state = 1;
+  sb.states_per_head = NC;
   sb.final_out = h_final;
   sb.NC = NC;
   sb.mode = d->dot_mode;
@@ -272,12 +271,13 @@ extern "C" gdn2_status gdn2_fwd(const gdn2_desc* d, const void* q, const void* k
 }
 
 extern "C" gdn2_status gdn2_bwd(const gdn2_desc* d, const void* q, const void* k, const void* v, const void* w,
-                                const void* b, const void* g, const void* residual, const float* d_o,
-                                const float* d_hfinal, void* dq, void* dk, void* dv, void* dw, void* db, void* dg,
-                                float* dh0, void* workspace, uint32_t* dev_status, void* stream) {
+                                const void* b, const void* g, const void* residual, const float* h_final,
+                                const float* d_o, const float* d_hfinal, void* dq, void* dk, void* dv, void* dw,
+                                void* db, void* dg, float* dh0, void* workspace, uint32_t* dev_status,
+                                void* stream) {
   gdn2_status s = check_desc(d);
   if (s != GDN2_OK) return s;
-  const void* ptrs[] = {q, k, v, w, b, g, d_o, dq, dk, dv, dw, db, dg, dh0};
+  const void* ptrs[] = {q, k, v, w, b, g, h_final, d_o, dq, dk, dv, dw, db, dg, dh0};
   for (const void* x : ptrs)
     if (!x || !aligned16(x)) return GDN2_ERR_INVALID_ARGUMENT;
   if ((d_hfinal && !aligned16(d_hfinal)) || !residual || !aligned256(residual) || !workspace ||
@@ -290,6 +290,7 @@ extern "C" gdn2_status gdn2_bwd(const gdn2_desc* d, const void* q, const void* k
   base.d_o = d_o;
   base.dq = dq; base.dk = dk; base.dv = dv; base.dw = dw; base.db = db; base.dg = dg;
   base.ws = static_cast<uint8_t*>(workspace);
+  base.h_final = h_final;
   const int BH = d->B * d->H, NC = base.op.NC;
   base.wl = ws_layout(BH, NC, mode_from_enum(d->b3_dot_mode));
 
@@ -300,7 +301,6 @@ extern "C" gdn2_status gdn2_bwd(const gdn2_desc* d, const void* q, const void* k
   sb.state_in = d_hfinal;
   sb.states = reinterpret_cast<float*>(base.ws + base.wl.dhs);
   sb.states_per_head = NC;
-  sb.store_final_state = 0;
   sb.final_out = dh0;
   sb.NC = NC;
   sb.mode = d->b3_dot_mode;

@@ -244,8 +244,9 @@ __global__ void __launch_bounds__(kCT, 1) bwd_intra_kernel(const BwdParams P) {
   TIn* dg = reinterpret_cast<TIn*>(P.dg) + off;
   const size_t mat = (size_t)kT * kD;
   const float* ainv_g = reinterpret_cast<const float*>(p.res + p.rl.ainv) + (size_t)ch * mat;
-  const float* hpre_g = reinterpret_cast<const float*>(p.res + p.rl.hs) + ((size_t)bh * (p.NC + 1) + c) * mat;
-  const float* hnext_g = hpre_g + mat;
+  const float* hpre_g = reinterpret_cast<const float*>(p.res + p.rl.hs) + ((size_t)bh * p.NC + c) * mat;
+  // h after this chunk: the next chunk's stored entry state, or the call's final state
+  const float* hnext_g = c + 1 < p.NC ? hpre_g + mat : P.h_final + (size_t)bh * mat;
   const float* vnew_g = reinterpret_cast<const float*>(p.res + p.rl.vnew) + (size_t)ch * mat;
   const float* dvl_g = reinterpret_cast<const float*>(P.ws + P.wl.dvl) + (size_t)ch * mat;
   const float* dhn_g = reinterpret_cast<const float*>(P.ws + P.wl.dhs) + (size_t)ch * mat;

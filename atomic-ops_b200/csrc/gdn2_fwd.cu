@@ -403,7 +403,7 @@ __global__ void __launch_bounds__(kCT, 1) fwd_out_kernel(const OpParams p, float
   const float* aqk_g = reinterpret_cast<const float*>(p.res + p.rl.aqk) + (size_t)ch * mat;
   const float* wp_g = reinterpret_cast<const float*>(p.res + p.rl.wp) + (size_t)ch * mat;
   const float* u_g = reinterpret_cast<const float*>(p.fws + p.rl.u) + (size_t)ch * mat;
-  const float* h_g = reinterpret_cast<const float*>(p.res + p.rl.hs) + ((size_t)bh * (p.NC + 1) + c) * mat;
+  const float* h_g = reinterpret_cast<const float*>(p.res + p.rl.hs) + ((size_t)bh * p.NC + c) * mat;
   float* vn_g = reinterpret_cast<float*>(p.res + p.rl.vnew) + (size_t)ch * mat;
   float* o_g = o_out + off;
   const Mode md = mode_from_enum(DOT >= 0 ? DOT : p.dot_mode);

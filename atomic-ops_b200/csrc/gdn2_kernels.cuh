@@ -36,7 +36,7 @@ __host__ __device__ inline ResLayout res_layout(int BH, int NC, Mode fwd_scan) {
   r.aqk = o; o = align256(o + nch * mat);
   r.ainv = o; o = align256(o + nch * mat);
   r.wp = o; o = align256(o + nch * mat);
-  r.hs = o; o = align256(o + (size_t)BH * (NC + 1) * mat);  // h entering each chunk, then h_final
+  r.hs = o; o = align256(o + (size_t)BH * NC * mat);  // h entering each chunk (h_final is the output)
   r.vnew = o; o = align256(o + nch * mat);
   r.wide = o; o = align256(o + nch * sizeof(int));  // per chunk-head: 1 if it has wide channels
   r.total = o;
@@ -708,8 +708,7 @@ struct ScanParams {
   const float* add;        // per-chunk 128x128 additive term (Bc or Cc)
   const float* state_in;   // (BH, D, D) initial state, or nullptr for zeros
   float* states;           // per-chunk stored states: states[(bh * states_per_head + c) * D * D]
-  int states_per_head;     // NC + 1 (forward) or NC (backward)
-  int store_final_state;   // also store the final state at slot NC (forward)
+  int states_per_head;     // NC
   float* final_out;        // (BH, D, D)
   int NC;
   int mode;                // gdn2_precision of the products
@@ -732,6 +731,7 @@ struct BwdParams {
   void* dq; void* dk; void* dv; void* dw; void* db; void* dg;  // (B,H,L,D) in the input dtype
   uint8_t* ws;             // backward workspace
   WsLayout wl;
+  const float* h_final;    // (BH, D, D) the forward's final state: h after the last chunk
 };
 cudaError_t launch_bwd_pre(const BwdParams& p, bool bf16, int nblocks, cudaStream_t st);
 cudaError_t launch_bwd_intra(const BwdParams& p, bool bf16, int nblocks, cudaStream_t st);

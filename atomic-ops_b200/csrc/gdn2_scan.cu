@@ -128,11 +128,6 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanParams sp) 
     float* dst = sp.final_out + (size_t)bh * mat + (size_t)t * kD + v0;
 #pragma unroll
     for (int j = 0; j < kDV; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(h[j], h[j + 1], h[j + 2], h[j + 3]);
-    if (sp.store_final_state) {
-      float* d2 = sp.states + ((size_t)bh * sp.states_per_head + sp.NC) * mat + (size_t)t * kD + v0;
-#pragma unroll
-      for (int j = 0; j < kDV; j += 4) *reinterpret_cast<float4*>(d2 + j) = make_float4(h[j], h[j + 1], h[j + 2], h[j + 3]);
-    }
   }
   tc_fence_before();
   __syncthreads();
