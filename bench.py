@@ -826,6 +826,25 @@ def run_lm(args):
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(f0.elapsed_time(f1) / steps)
     final_loss = float(loss)
+    # the data-parallel gradient all-reduce on its own: one all-reduce of a buffer the size of all
+    # gradients (the DDP buckets' total), timed on the device, max over ranks; set beside the
+    # 1-GPU step time it tells how much of it the backward pass hides
+    allreduce_ms = None
+    if dist is not None:
+        nbytes = sum(p_.numel() for p_ in model.parameters())
+        buf = torch.ones(nbytes, device=dev)
+        for _ in range(3):
+            dist.all_reduce(buf)
+        torch.cuda.synchronize()
+        dist.barrier()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        for _ in range(10):
+            dist.all_reduce(buf)
+        a1.record()
+        torch.cuda.synchronize()
+        allreduce_ms = max_over_ranks(a0.elapsed_time(a1) / 10)
+        del buf
     if args.torch_profile:      # every rank steps (the DDP all-reduce is collective); rank 0 prints
         from torch.profiler import ProfilerActivity, profile
         with profile(activities=[ProfilerActivity.CUDA]) as tp:
@@ -855,6 +874,7 @@ def run_lm(args):
             "gpu_launches": (op_launches(LM_B * mc["n_heads"], LM_L, cfg) + 2) * len(model.layers) * steps,
             "final_loss": final_loss,
             "published_other_model_ms": LM_PUBLISHED_MS_OTHER_MODEL,
+            "grad_allreduce_alone_ms": allreduce_ms,
             "clocks": clk, "device_status": status,
         }
         print(json.dumps(line), flush=True)
