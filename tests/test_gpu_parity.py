@@ -308,3 +308,29 @@ def test_stuck_wait_ends_as_status_and_context_survives():
     want = _run_oracle(cfg, xs, h0)
     _compare(got, want, 1e-4)
     assert atomic_gdn2.last_status() == 0
+
+
+def test_async_status_check_reports_at_a_later_call():
+    """The default status check never stalls the host: a call whose kernels flag a problem (here a
+    positive gate, outside domain I-1) returns normally, and the next call raises once the
+    asynchronous copy of the status word has landed; after that the word is clear again."""
+    cfg = make_cfg()
+    xs, _ = O.bench_inputs(1, 1, 128, D, 0)
+    bad = [t.cuda() for t in xs]
+    bad[5] = bad[5].abs()
+    good = [t.cuda() for t in xs]
+    fn = make_blr_trainable(cfg, 0.1)
+    atomic_gdn2.set_checks("async")
+    try:
+        with torch.no_grad():
+            fn(*bad)                      # flagged on the device, not raised here
+            torch.cuda.synchronize()      # the status copy has landed
+            with pytest.raises(RuntimeError, match="reported at a later call"):
+                fn(*good)
+            torch.cuda.synchronize()
+            fn(*good)                     # the word was cleared when the error was raised
+            torch.cuda.synchronize()
+            fn(*good)
+        assert atomic_gdn2.last_status() == 0
+    finally:
+        atomic_gdn2.set_checks(True)
