@@ -82,6 +82,7 @@ class _DevStatus:
     def __init__(self, dev: torch.device):
         self.word = torch.zeros(1, dtype=torch.int32, device=dev)
         self.host = torch.zeros(self.NSLOT, dtype=torch.int32, pin_memory=True)
+        self.events = [torch.cuda.Event() for _ in range(self.NSLOT)]   # one per host slot, reused
         self.pending = collections.deque()      # (event, slot, what)
         self.next_slot = 0
 
@@ -147,7 +148,7 @@ def _after_call(st: _DevStatus, what: str) -> None:
     slot = st.next_slot
     st.next_slot = (slot + 1) % st.NSLOT
     st.host[slot:slot + 1].copy_(st.word, non_blocking=True)
-    ev = torch.cuda.Event()
+    ev = st.events[slot]
     ev.record()
     st.pending.append((ev, slot, what))
 
