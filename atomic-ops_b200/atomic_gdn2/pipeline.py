@@ -14,14 +14,16 @@ place of jax.custom_vjp:
   result is bit-identical to one launch sequence per segment, because the scans store and reload
   the carried state unchanged at a boundary and every other kernel is chunk-local.  Residuals
   are the same size either way (the reference also keeps every segment's residuals);
-* inside the library the heads are split into batch groups (gdn2_set_batch_groups, default 4,
-  environment GDN2_STREAMS) whose launch sequences run on forked side streams joined back to the
-  caller's stream, so one group's low-occupancy scans and last-wave tails overlap the other
-  groups' chunk kernels; the host issues one C call per segment group in each direction;
+* inside the library the heads are split into batch groups (gdn2_set_batch_groups, default 6,
+  environment GDN2_STREAMS; one group when all chunk-heads fit in one wave of the SMs) whose launch
+  sequences run on forked side streams joined back to the caller's stream, so one group's
+  low-occupancy scans and last-wave tails overlap the other groups' chunk kernels; the host issues
+  one C call per segment group in each direction;
 * device status: every call ORs its status bits (a bounded on-chip wait that ran out, a positive
   gate) into one persistent status word per device.  By default the word is checked without
-  stalling the host: after each call an asynchronous copy of it goes to pinned host memory, and a
-  later call raises once that copy has landed with a bit set (last_status() reads the word).  GDN2_CHECK=sync
+  stalling the host: an asynchronous copy of it goes to pinned host memory (one copy in flight at
+  a time; the word is cumulative, so a copy covers every call before it), and a later call raises
+  once a copy has landed with a bit set (last_status() reads the word).  GDN2_CHECK=sync
   (or set_checks(True)) synchronises after every call and raises at once; GDN2_CHECK=0 turns the
   checks off.  Nothing is checked while a stream is being captured into a CUDA graph (the word
   still collects the replays' bits: read it with last_status());
@@ -75,16 +77,15 @@ def set_checks(enabled) -> None:
 
 
 class _DevStatus:
-    """The persistent status word of one device and the in-flight asynchronous copies of it."""
-
-    NSLOT = 16
+    """The persistent status word of one device and its asynchronous host copy (at most one in
+    flight: the word is cumulative, so a copy covers every call issued before it)."""
 
     def __init__(self, dev: torch.device):
+        self.index = dev.index
         self.word = torch.zeros(1, dtype=torch.int32, device=dev)
-        self.host = torch.zeros(self.NSLOT, dtype=torch.int32, pin_memory=True)
-        self.events = [torch.cuda.Event() for _ in range(self.NSLOT)]   # one per host slot, reused
-        self.pending = collections.deque()      # (event, slot, what)
-        self.next_slot = 0
+        self.host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        self.event = torch.cuda.Event()
+        self.inflight = None      # the call whose copy is in flight, or None
 
 
 _status = {}
@@ -131,34 +132,35 @@ def _after_call(st: _DevStatus, what: str) -> None:
         code = int(st.word.item())
         if code:
             st.word.zero_()
-            st.pending.clear()
+            st.inflight = None
             raise RuntimeError(_status_message(code, what))
         return
-    # async: report copies that have landed, then queue this call's copy
-    while st.pending and st.pending[0][0].query():
-        _, slot, w = st.pending.popleft()
-        code = int(st.host[slot])
+    # async: report the copy in flight once it has landed, then start a new one covering this call
+    if st.inflight is not None:
+        if not st.event.query():
+            return                    # not landed yet: that copy or a later one reports this call
+        code, w = int(st.host[0]), st.inflight
+        st.inflight = None
         if code:
             st.word.zero_()
-            st.pending.clear()
             raise RuntimeError(_status_message(code, f"{w} (reported at a later call)"))
-    if len(st.pending) == st.NSLOT:          # every slot in flight: wait for the oldest
-        st.pending[0][0].synchronize()
-        return _after_call(st, what)
-    slot = st.next_slot
-    st.next_slot = (slot + 1) % st.NSLOT
-    st.host[slot:slot + 1].copy_(st.word, non_blocking=True)
-    ev = st.events[slot]
-    ev.record()
-    st.pending.append((ev, slot, what))
+    st.host.copy_(st.word, non_blocking=True)
+    st.event.record(_cur_stream(st.index))
+    st.inflight = what
 
 
 def _ptr(t):
     return ctypes.c_void_p(0 if t is None else t.data_ptr())
 
 
-def _stream():
-    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+def _stream(index: int):
+    """The device's current CUDA stream as a raw handle (the fast path of current_stream())."""
+    return ctypes.c_void_p(torch._C._cuda_getCurrentRawStream(index))
+
+
+def _cur_stream(index: int) -> torch.cuda.Stream:
+    sid, di, dt = torch._C._cuda_getCurrentStream(index)
+    return torch.cuda.Stream(stream_id=sid, device_index=di, device_type=dt)
 
 
 def _make_desc(cfg: BLRConfig, scale: float, B, H, Lseg, D, stride_b, stride_h, dtype) -> _lib.Gdn2Desc:
@@ -238,7 +240,7 @@ class _GDN2(torch.autograd.Function):
         if B == 1:
             sb = max(sb, H * sh)
         el = q.element_size()
-        stream = _stream()
+        stream = _stream(dev.index)
         h = h0
         saved, finals = [], []
         plan = _plan(lib, cfg, scale, B, H, D, sb, sh, q.dtype, nc)
@@ -287,7 +289,7 @@ class _GDN2(torch.autograd.Function):
         dh0_all = torch.empty((B, H, D, D), dtype=torch.float32, device=dev)
         st = _dev_status(dev)
         el = q.element_size()
-        stream = _stream()
+        stream = _stream(dev.index)
         dh = dhf32
         n = len(ctx.plan)
         for si in range(n - 1, -1, -1):

@@ -147,7 +147,7 @@ constexpr int kMaxDevs = 64;
 
 int initial_groups() {
   const char* e = std::getenv("GDN2_STREAMS");
-  int n = e ? std::atoi(e) : 4;
+  int n = e ? std::atoi(e) : 6;
   return n < 1 ? 1 : (n > kMaxGroups ? kMaxGroups : n);
 }
 std::atomic<int> g_groups{initial_groups()};
@@ -179,12 +179,25 @@ DevStreams* dev_streams(cudaStream_t caller) {
   return ok ? &ds : nullptr;
 }
 
-// Runs launch(group, first_head, n_heads, stream) for every group of the call's BH heads: on the
-// caller's stream for a single group, else on forked side streams.
+// Streaming multiprocessors of the current device (looked up once per device).
+int sm_count() {
+  static std::atomic<int> cache[kMaxDevs];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevs) return 0;
+  int n = cache[dev].load(std::memory_order_relaxed);
+  if (n == 0 && cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess) cache[dev].store(n);
+  return n;
+}
+
+// Runs launch(first_head, n_heads, stream) for every group of the call's BH heads: on the caller's
+// stream for a single group, else on forked side streams.  A call whose chunk-heads all fit in one
+// wave of the GPU's SMs (the chunk kernels run one CTA per chunk-head and per SM) runs as one group:
+// there is no wave tail for other groups to fill, and every group adds launches and events.
 template <class F>
-gdn2_status run_groups(int BH, cudaStream_t st, F launch) {
+gdn2_status run_groups(int BH, int NC, cudaStream_t st, F launch) {
   int G = g_groups.load(std::memory_order_relaxed);
   if (G > BH) G = BH;
+  if (G > 1 && (long long)BH * NC <= (long long)sm_count()) G = 1;
   DevStreams* ds = G > 1 ? dev_streams(st) : nullptr;
   if (!ds) G = 1;
   if (G == 1) return launch(0, BH, st) == cudaSuccess ? GDN2_OK : GDN2_ERR_CUDA;
@@ -256,7 +269,7 @@ extern "C" gdn2_status gdn2_fwd(const gdn2_desc* d, const void* q, const void* k
   sb.clip = d->clip;
   sb.status = dev_status;
 
-  return run_groups(BH, st, [&](int h_first, int nh, cudaStream_t gs) -> cudaError_t {
+  return run_groups(BH, NC, st, [&](int h_first, int nh, cudaStream_t gs) -> cudaError_t {
     OpParams p = base;
     p.fws = static_cast<uint8_t*>(workspace);
     p.ch0 = h_first * NC;
@@ -308,7 +321,7 @@ extern "C" gdn2_status gdn2_bwd(const gdn2_desc* d, const void* q, const void* k
   sb.clip = d->clip;
   sb.status = dev_status;
 
-  return run_groups(BH, st, [&](int h_first, int nh, cudaStream_t gs) -> cudaError_t {
+  return run_groups(BH, NC, st, [&](int h_first, int nh, cudaStream_t gs) -> cudaError_t {
     BwdParams bp = base;
     bp.op.ch0 = h_first * NC;
     cudaError_t e = timed(GDN2_K_BWD_PRE, gs, [&] { return launch_bwd_pre(bp, bf16, nh * NC, gs); });

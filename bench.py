@@ -45,12 +45,15 @@ CFG_KW = dict(bt=128, bc=64, score_bs=128, bs2=64, mb=8, wy_eps=0.0,
               dot_mode="highest", solve_dot_mode="bf16x3", b3_dot_mode="bf16x3")
 
 
-def op_launches(nbh, nl, cfg):
+def op_launches(nbh, nl, cfg, sms):
     """This library's kernel launches in one fwd+bwd operator call over nbh heads: per batch group
-    (one launch sequence per side stream) and segment group, fwd_intra (wide chunks included), the
-    forward scan, fwd_out, bwd_pre, the backward scan, bwd_intra and its wide-channel launch."""
+    (one launch sequence per side stream; one group when the chunk-heads fit in one wave of the
+    `sms` multiprocessors) and segment group, fwd_intra (wide chunks included), the forward scan,
+    fwd_out, bwd_pre, the backward scan, bwd_intra and its wide-channel launch."""
     from atomic_gdn2 import _lib
-    return 7 * min(_lib.batch_groups(), nbh) * math.ceil((nl // T) / cfg.max_chunks_per_call)
+    seg = min(nl // T, cfg.max_chunks_per_call)
+    groups = 1 if nbh * seg <= sms else min(_lib.batch_groups(), nbh)
+    return 7 * groups * math.ceil((nl // T) / cfg.max_chunks_per_call)
 
 
 def parse():
@@ -625,7 +628,8 @@ def run_ours(args):
                     "pipeline": "next step's H2D and previous step's D2H overlapped with this step's compute",
                     "host_buffers": ("pinned, on the GPU's local CPUs (NVML affinity, %d CPUs)" % len(local_cpus))
                     if local_cpus else "pinned"},
-            "gpu_launches": op_launches(nbh_local, L, cfg) * args.steps,
+            "gpu_launches": op_launches(nbh_local, L, cfg, torch.cuda.get_device_properties(dev).multi_processor_count)
+            * args.steps,
             "clocks": clk,
             "device_status": status,
         }
@@ -871,7 +875,9 @@ def run_lm(args):
             "operator_kernels_ms_per_step": op_ms,
             "operator_share": sum(op_ms.values()) / ms,  # of the timed (overlapped) step: an upper bound
             "e2e": {"value": e2e_ms, "unit": "ms", "h2d_bytes_per_step": LM_B * LM_L * 8, "d2h_bytes_per_step": 4},
-            "gpu_launches": (op_launches(LM_B * mc["n_heads"], LM_L, cfg) + 2) * len(model.layers) * steps,
+            "gpu_launches": (op_launches(LM_B * mc["n_heads"], LM_L, cfg,
+                                         torch.cuda.get_device_properties(dev).multi_processor_count) + 2)
+            * len(model.layers) * steps,
             "final_loss": final_loss,
             "published_other_model_ms": LM_PUBLISHED_MS_OTHER_MODEL,
             "grad_allreduce_alone_ms": allreduce_ms,

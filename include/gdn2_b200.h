@@ -124,8 +124,10 @@ gdn2_status gdn2_bwd(const gdn2_desc* desc, const void* q, const void* k, const 
  * launch sequences run on side streams the library owns, forked from the caller's stream by an
  * event and joined back to it before the call returns (capturable into a CUDA graph; the streams
  * are created by the first multi-group call on a device, which must not be under capture -- a call
- * under capture before that runs as one group).  Results do not depend on n.  n is clamped to
- * [1, 8]; the initial value is the environment's GDN2_STREAMS, else 4.  Returns the previous value. */
+ * under capture before that runs as one group).  A call whose B*H*(L/128) chunk-heads fit in one
+ * wave of the GPU's multiprocessors runs as one group whatever n is.  Results do not depend on the
+ * grouping.  n is clamped to [1, 8]; the initial value is the environment's GDN2_STREAMS, else 6.
+ * Returns the previous value. */
 int32_t gdn2_set_batch_groups(int32_t n);
 int32_t gdn2_get_batch_groups(void);
 

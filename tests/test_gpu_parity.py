@@ -155,10 +155,11 @@ def test_segment_grouping_is_exact(monkeypatch):
 
 def test_batch_groups_do_not_change_results():
     """The library's batch groups (heads split over forked side streams) only change the schedule:
-    one, two, three and eight groups give bit-identical o, h_final and gradients."""
+    one, two, three and eight groups give bit-identical o, h_final and gradients (a problem of 160
+    chunk-heads, more than one wave of the SMs, so that the groups are used)."""
     from atomic_gdn2 import _lib
     cfg = make_cfg()
-    xs, h0 = O.bench_inputs(2, 3, 384, D, 6)
+    xs, h0 = O.bench_inputs(2, 5, 2048, D, 6)
     prev = _lib.set_batch_groups(1)
     try:
         ref = _run_op(cfg, xs, h0)
