@@ -17,6 +17,10 @@ constexpr uint32_t kScanImg = 2 * 65536;                 // largest image (tf32,
 constexpr uint32_t kScanB = 2 * 16384;                   // state tile hi + lo
 constexpr uint32_t kScanSmem = 1024 + kScanImg + kScanB + 64;
 
+// Transition images arrive by bulk copy.  When two images fit in the image area (every mode but
+// 3 x tf32, whose hi + lo image fills it), they are double-buffered: chunk c + 1's image is copied
+// while chunk c is computed, instead of after chunk c's MMA has released the one buffer.
+
 
 
 __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanParams sp) {
@@ -25,9 +29,9 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanParams sp) 
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* img_s = sm;
   uint8_t* b_s = sm + kScanImg;
-  uint64_t* bar_ld = reinterpret_cast<uint64_t*>(sm + kScanImg + kScanB);
-  uint64_t* bar_mma = bar_ld + 1;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_ld + 2);
+  uint64_t* bar_ld = reinterpret_cast<uint64_t*>(sm + kScanImg + kScanB);  // one per image buffer
+  uint64_t* bar_mma = bar_ld + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_ld + 3);
 
   const int t = threadIdx.x, warp = t >> 5;
   const int tiles = kD / kDV;
@@ -35,6 +39,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanParams sp) 
   const Mode m = mode_from_enum(sp.mode);
   const uint32_t part = image_part_bytes(m);
   const uint32_t ibytes = image_bytes(m);
+  const int nbuf = 2 * ibytes <= kScanImg ? 2 : 1;
   const bool lo = m.passes == 3;
   const size_t mat = (size_t)kD * kD;
 
@@ -43,7 +48,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanParams sp) 
     tmem_relinquish();
   }
   if (t == 0) {
-    mbar_init(bar_ld, 1);
+    mbar_init(&bar_ld[0], 1);
+    mbar_init(&bar_ld[1], 1);
     mbar_init(bar_mma, 1);
     fence_mbar_init();
   }
@@ -53,12 +59,17 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanParams sp) 
   const uint32_t tb = *tslot;
 
   auto chunk_of = [&](int it) { return sp.reverse ? sp.NC - 1 - it : it; };
-  auto issue_load = [&](int c) {
-    const uint8_t* src = sp.img + ((size_t)bh * sp.NC + c) * sp.img_stride;
-    mbar_arrive_expect_tx(bar_ld, ibytes);
-    for (uint32_t o = 0; o < ibytes; o += 32768u) bulk_g2s(img_s + o, src + o, 32768u, bar_ld);
+  auto issue_load = [&](int it) {  // the image of iteration it into its buffer
+    const int bf = nbuf == 2 ? (it & 1) : 0;
+    const uint8_t* src = sp.img + ((size_t)bh * sp.NC + chunk_of(it)) * sp.img_stride;
+    uint8_t* dst = img_s + (uint32_t)bf * ibytes;
+    mbar_arrive_expect_tx(&bar_ld[bf], ibytes);
+    for (uint32_t o = 0; o < ibytes; o += 32768u) bulk_g2s(dst + o, src + o, 32768u, &bar_ld[bf]);
   };
-  if (t == 0) issue_load(chunk_of(0));
+  if (t == 0) {
+    issue_load(0);
+    if (nbuf == 2 && sp.NC > 1) issue_load(1);
+  }
 
   // State row t, columns v0 .. v0+31.
   float h[kDV];
@@ -74,13 +85,15 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanParams sp) 
     for (int j = 0; j < kDV; ++j) h[j] = 0.f;
   }
 
-  const Tile A[2] = {tile_k(smem_u32(img_s), 128u * (uint32_t)esize(m)),
-                     tile_k(smem_u32(img_s) + part, 128u * (uint32_t)esize(m))};
+  const Tile A0[2] = {tile_k(smem_u32(img_s), 128u * (uint32_t)esize(m)),
+                      tile_k(smem_u32(img_s) + part, 128u * (uint32_t)esize(m))};
+  const Tile A1[2] = {tile_k(smem_u32(img_s) + ibytes, 128u * (uint32_t)esize(m)),
+                      tile_k(smem_u32(img_s) + ibytes + part, 128u * (uint32_t)esize(m))};
   const uint32_t bpart = (m.fmt == kTF32) ? 16384u : 8192u;
   const Tile Bt[2] = {tile_mn(smem_u32(b_s), kDV * (uint32_t)esize(m), m.fmt),
                       tile_mn(smem_u32(b_s) + bpart, kDV * (uint32_t)esize(m), m.fmt)};
   const int nsteps = 128 * esize(m) / 32;
-  uint32_t ph_ld = 0, ph_mma = 0;
+  uint32_t ph_ld[2] = {0u, 0u}, ph_mma = 0;
 
   for (int it = 0; it < sp.NC; ++it) {
     const int c = chunk_of(it);
@@ -104,18 +117,20 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanParams sp) 
       }
     }
     staged_sync();
-    mbar_wait(bar_ld, ph_ld, sp.status);
-    ph_ld ^= 1u;
+    const int bf = nbuf == 2 ? (it & 1) : 0;
+    mbar_wait(&bar_ld[bf], ph_ld[bf], sp.status);
+    ph_ld[bf] ^= 1u;
     if (t == 0) {
       tc_fence_after();
-      mma_tiles(m.fmt, m.passes, tb, A, Bt, kDV, nsteps, false, false);
+      mma_tiles(m.fmt, m.passes, tb, bf ? A1 : A0, Bt, kDV, nsteps, false, false);
       mma_commit(bar_mma);
     }
     __syncwarp();  // park warp 0's other lanes here while lane 0 issues, instead of polling the barrier
     mbar_wait(bar_mma, ph_mma, sp.status);
     ph_mma ^= 1u;
     tc_fence_after();
-    if (t == 0 && it + 1 < sp.NC) issue_load(chunk_of(it + 1));
+    // the buffer this MMA read is free: the image nbuf iterations ahead goes into it
+    if (t == 0 && it + nbuf < sp.NC) issue_load(it + nbuf);
     float acc[32];
     tmem_ld32(tb, 0, acc);
 #pragma unroll
