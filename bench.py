@@ -98,7 +98,39 @@ def make_inputs(seed, device, dtype, shape=(B, H, L)):
 MODE_COST = {"highest": 6.0, "bf16x3": 3.0, "default": 1.0, "tf32": 2.0}
 
 
-def kernel_work(s_in, nc, modes):
+def mode_cost(tf32_ratio):
+    """MODE_COST with the tf32 modes charged at a measured bf16 / tf32 throughput ratio."""
+    return {"highest": 3.0 * tf32_ratio, "bf16x3": 3.0, "default": 1.0, "tf32": tf32_ratio}
+
+
+def measured_tf32_tflops(dev):
+    """Dense TF32 tensor-core throughput of this GPU, measured like MEASURED_PEAKS.json's bf16
+    figure: a library fp32 GEMM with TF32 allowed, 8192^3 (2 N^3 FLOPs), best of 10 after warm-up,
+    CUDA events.  Returns TFLOP/s."""
+    n = 8192
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    try:
+        a = torch.randn(n, n, device=dev)
+        b = torch.randn(n, n, device=dev)
+        c = torch.empty(n, n, device=dev)
+        for _ in range(3):
+            torch.matmul(a, b, out=c)
+        best = float("inf")
+        for _ in range(10):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch.matmul(a, b, out=c)
+            e1.record()
+            torch.cuda.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+        del a, b, c
+        return 2.0 * n ** 3 / (best / 1e3) / 1e12
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+def kernel_work(s_in, nc, modes, cost=MODE_COST):
     """Per chunk-head: (algorithmic FLOPs, bf16-equivalent MMA FLOPs in the configured modes,
     compulsory HBM bytes) of each kernel.  The FLOPs are the reference algorithm's dense GEMM count
     split over the kernels that perform its parts; B4 (four T^2 D products of bwd_intra) is
@@ -107,8 +139,8 @@ def kernel_work(s_in, nc, modes):
     td2 = T * D * D
     t3 = T ** 3
     td = T * D
-    dot, sol, b3 = (MODE_COST[modes[k]] for k in ("dot_mode", "solve_dot_mode", "b3_dot_mode"))
-    hi = MODE_COST["highest"]
+    dot, sol, b3 = (cost[modes[k]] for k in ("dot_mode", "solve_dot_mode", "b3_dot_mode"))
+    hi = cost["highest"]
     f_fi, f_bi = 2 * 4 * t2d + (2 / 3) * t3, 2 * (10 * t2d + 3 * td2 + 2 * t3)
     return {
         "fwd_intra": (f_fi, 2 * 4 * t2d * dot + (2 / 3) * t3 * sol, 6 * s_in * td),
@@ -556,7 +588,8 @@ def run_ours(args):
     if rank == 0:
         hbm, tf_burst, tf_sust, peak_kind = peaks()
         modes = {k: cfg.__dict__[k] for k in ("dot_mode", "solve_dot_mode", "b3_dot_mode")}
-        work = kernel_work(s_in, L // T, modes)
+        tf32 = measured_tf32_tflops(dev)
+        work = kernel_work(s_in, L // T, modes, mode_cost(tf_burst / tf32))
         nch = nbh_local * (L // T)
         traffic = ncu_traffic() if (dtype == torch.float32 and world == 1) else {}
         kern = {}
@@ -612,8 +645,10 @@ def run_ours(args):
                                        "compulsory bytes at the measured HBM rate",
                          "step_frac": t_step_roof / ms,
                          "mode_adjusted_estimate": {
-                             "note": "unmeasured estimate: each FLOP at its precision mode's MMA cost in bf16-MMA "
-                                     "equivalents (3 x tf32 = 6, 3 x bf16 = 3, bf16 = 1)",
+                             "note": "each FLOP charged its precision mode's MMA cost in bf16-MMA equivalents: "
+                                     "3 x bf16 = 3, bf16 = 1, tf32 = the measured bf16 / tf32 GEMM throughput "
+                                     "ratio, 3 x tf32 = 3 x that ratio",
+                             "tf32_tflops_measured": tf32, "bf16_over_tf32": tf_burst / tf32,
                              "kernel_frac": kd["t_mode_ms"] / kd["ms_per_launch"],
                              "step_frac": t_step_mode / ms}},
             "kernels": {n: {"ms": round(v["ms_per_launch"], 4), "share": round(v["share"], 3),
