@@ -35,7 +35,6 @@ include/gdn2_b200.h.  PyTorch only provides device memory, streams and autograd 
 """
 from __future__ import annotations
 
-import collections
 import ctypes
 import os
 
