@@ -21,8 +21,6 @@ constexpr uint32_t kScanSmem = 1024 + kScanImg + kScanB + 64;
 // 3 x tf32, whose hi + lo image fills it), they are double-buffered: chunk c + 1's image is copied
 // while chunk c is computed, instead of after chunk c's MMA has released the one buffer.
 
-
-
 __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanParams sp) {
   pdl_enter();
   extern __shared__ uint8_t smem_raw[];
@@ -116,10 +114,16 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanParams sp) 
         add[j] = x.x; add[j + 1] = x.y; add[j + 2] = x.z; add[j + 3] = x.w;
       }
     }
-    staged_sync();
+    // Every thread sees this chunk's image land BEFORE the CTA barrier; the buffer is refilled
+    // only after that barrier, so no thread can still be waiting on a phase when the next one
+    // completes (a thread that tested the parity after the refill had landed would see it come
+    // round again and wait for a phase that never completes).  Waiting in every thread here is
+    // also faster than letting the issuing thread wait alone (measured: 0.059 against 0.070 ms
+    // per forward scan of B4 H6 L2048, fp32).
     const int bf = nbuf == 2 ? (it & 1) : 0;
     mbar_wait(&bar_ld[bf], ph_ld[bf], sp.status);
     ph_ld[bf] ^= 1u;
+    staged_sync();
     if (t == 0) {
       tc_fence_after();
       mma_tiles(m.fmt, m.passes, tb, bf ? A1 : A0, Bt, kDV, nsteps, false, false);

@@ -311,6 +311,21 @@ def run_reference(args):
 # --------------------------------------------------------------------------------------
 # our arm
 # --------------------------------------------------------------------------------------
+def status_gate(step, inputs, dist, max_over_ranks):
+    """One step, then every rank's device status word read and reduced over the ranks: all ranks
+    stop together when any word has a bit set, so that no rank is left alone in a collective."""
+    import atomic_gdn2
+    from atomic_gdn2.pipeline import _status_message
+    atomic_gdn2.set_checks(False)
+    step(inputs)
+    torch.cuda.synchronize()
+    code = int(max_over_ranks(float(atomic_gdn2.last_status())))
+    if code:
+        if dist is not None:
+            dist.destroy_process_group()
+        raise RuntimeError(_status_message(code, "first step (any rank)"))
+
+
 def _time_graph(step, xs_base, dev, warmup, steps, flush=None):
     """Capture step(leaf inputs) once into a CUDA graph on a side stream (leaf tensors and warm-up
     live on the capture stream, so autograd's per-stream bookkeeping stays inside the capture).
@@ -387,16 +402,16 @@ def run_ours(args):
         grads = torch.autograd.grad(loss, inputs)
         return loss, grads
 
-    # correctness gate on this device before timing (device status word must stay clean)
-    atomic_gdn2.set_checks(True)
-    step(xs)
-    atomic_gdn2.set_checks(False)
+    # correctness gate on every device before timing (device status words must stay clean)
+    status_gate(step, xs, dist, max_over_ranks)
 
     for _ in range(args.warmup):
         step(xs)
     # eager timing (every launch issued by the host each step; device status checks at their
-    # default, asynchronous setting, as a drop-in caller gets them)
-    atomic_gdn2.set_checks("async")
+    # default, asynchronous setting, as a drop-in caller gets them -- on one rank only: with
+    # several ranks an error raised on one of them would leave the others alone in a collective,
+    # so there the words are read after the loops and reduced over the ranks)
+    atomic_gdn2.set_checks("async" if dist is None else False)
     barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -795,6 +810,14 @@ def run_lm(args):
     if world > 1:
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    def max_over_ranks(x):
+        if dist is None:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
     # dense layers in TF32 on the tensor cores (fp32 storage and accumulation)
     torch.backends.cuda.matmul.allow_tf32 = True
     cfg = make_cfg()
@@ -811,9 +834,10 @@ def run_lm(args):
     def tokens():
         return torch.randint(0, mc["vocab"], (LM_B, LM_L), generator=gen, device=dev)
 
-    atomic_gdn2.set_checks(True)
-    step(tokens())
-    atomic_gdn2.set_checks("async")    # the default a drop-in caller gets: no host synchronisation
+    status_gate(step, tokens(), dist, max_over_ranks)
+    # the default a drop-in caller gets (no host synchronisation) on one rank; with several ranks
+    # the words are read after the loops and reduced, so that no rank leaves a collective alone
+    atomic_gdn2.set_checks("async" if dist is None else False)
     steps, warmup = max(1, min(args.steps, 20)), max(3, args.warmup)
     batches = [tokens() for _ in range(steps)]
     for _ in range(warmup):
@@ -833,15 +857,6 @@ def run_lm(args):
         dist.barrier()
     clk = clocks.stop()
     ms = e0.elapsed_time(e1) / steps
-    status = atomic_gdn2.last_status()
-
-    def max_over_ranks(x):
-        if dist is None:
-            return x
-        t = torch.tensor([x], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
     ms = max_over_ranks(ms)
     # operator kernels inside one step, with each operator call's batch as one launch sequence so
     # that launches do not overlap and their durations add up (the timed steps overlap the batch
@@ -884,6 +899,8 @@ def run_lm(args):
         torch.cuda.synchronize()
         allreduce_ms = max_over_ranks(a0.elapsed_time(a1) / 10)
         del buf
+    # every call since the gate: timed steps, profiled step and end-to-end steps, any rank
+    status = int(max_over_ranks(float(atomic_gdn2.last_status())))
     if args.torch_profile:      # every rank steps (the DDP all-reduce is collective); rank 0 prints
         from torch.profiler import ProfilerActivity, profile
         with profile(activities=[ProfilerActivity.CUDA]) as tp:
@@ -926,6 +943,11 @@ def run_lm(args):
 
 def main():
     args = parse()
+    # Multi-rank runs keep NCCL off NVLink multicast (NVLS): a rank that dies while its memory is
+    # bound to a multicast object raises NVLink faults on the other ranks' GPUs.  The operator's
+    # only collectives are the timing barrier and scalar reductions; the LM's gradient all-reduce
+    # runs over plain peer copies.
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     if args.workload == "lm":
         if args.impl == "reference":
             if int(os.environ.get("RANK", "0")) == 0:
