@@ -277,6 +277,7 @@ extern "C" gdn2_status gdn2_fwd(const gdn2_desc* d, const void* q, const void* k
     if (e != cudaSuccess) return e;
     ScanParams sp = sb;
     sp.bh0 = h_first;
+    sp.store_late = nh == BH;  // one batch group: the scan runs with no other group's kernels beside it
     e = timed(GDN2_K_FWD_SCAN, gs, [&] { return launch_scan(sp, nh, gs); });
     if (e != cudaSuccess) return e;
     return timed(GDN2_K_FWD_OUT, gs, [&] { return launch_fwd_out(p, bf16, o, nh * NC, gs); });
@@ -328,6 +329,7 @@ extern "C" gdn2_status gdn2_bwd(const gdn2_desc* d, const void* q, const void* k
     if (e != cudaSuccess) return e;
     ScanParams sp = sb;
     sp.bh0 = h_first;
+    sp.store_late = nh == BH;
     e = timed(GDN2_K_BWD_SCAN, gs, [&] { return launch_scan(sp, nh, gs); });
     if (e != cudaSuccess) return e;
     return timed(GDN2_K_BWD_INTRA, gs, [&] { return launch_bwd_intra(bp, bf16, nh * NC, gs); });

@@ -716,6 +716,7 @@ struct ScanParams {
   float clip;
   unsigned* status;
   int bh0;                 // first head of this launch
+  int store_late;          // store each chunk's entering state under its MMA (launch runs alone)
 };
 
 // Descriptor validation shared by every C-ABI entry point (gdn2_api.cu).
