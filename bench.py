@@ -692,7 +692,8 @@ def run_ours(args):
                              "step_frac": t_step_mode / ms}},
             "kernels": {n: {"ms": round(v["ms_per_launch"], 4), "share": round(v["share"], 3),
                             "bound": v["bound"], "roof_ms": round(v["t_roof_ms"], 4),
-                            "frac": round(v["t_roof_ms"] / v["ms_per_launch"], 4)} for n, v in kern.items()},
+                            "frac": round(v["t_roof_ms"] / v["ms_per_launch"], 4),
+                            "ncu_dram_bytes": traffic.get(n)} for n, v in kern.items()},
             "protocol": protocol,
             "weak": weak,
             "cpu_baseline": cpu,
