@@ -156,7 +156,8 @@ def test_segment_grouping_is_exact(monkeypatch):
 def test_batch_groups_do_not_change_results():
     """The library's batch groups (heads split over forked side streams) only change the schedule:
     one, two, three and eight groups give bit-identical o, h_final and gradients (a problem of 160
-    chunk-heads, more than one wave of the SMs, so that the groups are used)."""
+    chunk-heads, more than one wave of the SMs, so that the groups are used).  One group also
+    switches the scans to storing each chunk's entering state under the chunk's MMA."""
     from atomic_gdn2 import _lib
     cfg = make_cfg()
     xs, h0 = O.bench_inputs(2, 5, 2048, D, 6)
