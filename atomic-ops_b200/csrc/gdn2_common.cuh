@@ -548,20 +548,36 @@ __device__ __forceinline__ void stage_mnrow(const Tile& hi, const Tile& lo, bool
 // batch group's stream uses to fill this kernel's wave tail (measured 3 % slower).
 __device__ __forceinline__ void pdl_enter() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 // Launch `kern` with programmatic stream serialization (its body must begin with pdl_enter()).
+// The same, at the device's greatest scheduling priority when `urgent` (pending CTAs of urgent
+// launches are dispatched ahead of other streams' pending CTAs).
 template <class... KArgs, class... Args>
-static inline cudaError_t launch_pdl(void (*kern)(KArgs...), unsigned nblocks, unsigned nthreads, size_t smem,
-                                     cudaStream_t st, Args... args) {
+static inline cudaError_t launch_pdl_prio(void (*kern)(KArgs...), unsigned nblocks, unsigned nthreads, size_t smem,
+                                          cudaStream_t st, bool urgent, Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(nblocks);
   cfg.blockDim = dim3(nthreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute at[1];
+  cudaLaunchAttribute at[2];
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
+  if (urgent) {
+    static const int greatest = [] {
+      int least = 0, g = 0;
+      return cudaDeviceGetStreamPriorityRange(&least, &g) == cudaSuccess ? g : 0;
+    }();
+    at[1].id = cudaLaunchAttributePriority;
+    at[1].val.priority = greatest;
+    cfg.numAttrs = 2;
+  }
   return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+template <class... KArgs, class... Args>
+static inline cudaError_t launch_pdl(void (*kern)(KArgs...), unsigned nblocks, unsigned nthreads, size_t smem,
+                                     cudaStream_t st, Args... args) {
+  return launch_pdl_prio(kern, nblocks, nthreads, smem, st, false, args...);
 }
 
 }  // namespace gdn2
