@@ -168,8 +168,7 @@ DevStreams* dev_streams(cudaStream_t caller) {
   DevStreams& ds = g_dev_streams[dev];
   std::lock_guard<std::mutex> g(ds.mu);
   if (ds.ready) return &ds;
-  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-  if (cudaStreamIsCapturing(caller, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) return nullptr;
+  if (!stream_eager(caller)) return nullptr;
   bool ok = cudaEventCreateWithFlags(&ds.fork, cudaEventDisableTiming) == cudaSuccess;
   for (int i = 0; ok && i < kMaxGroups; ++i) {
     ok = cudaStreamCreateWithFlags(&ds.side[i], cudaStreamNonBlocking) == cudaSuccess &&

@@ -540,6 +540,18 @@ __device__ __forceinline__ void stage_mnrow(const Tile& hi, const Tile& lo, bool
   }
 }
 
+// True when `st` is not being captured into a CUDA graph.  A failed query (the legacy stream
+// while another thread captures in global mode) counts as capturing, and its error is cleared so
+// that the launch's own error check does not report it.
+inline bool stream_eager(cudaStream_t st) {
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cap) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return false;
+  }
+  return cap == cudaStreamCaptureStatusNone;
+}
+
 // Programmatic dependent launch: the chunk and scan kernels are launched with programmatic stream
 // serialization, which lets the hardware begin a launch before its predecessor in the stream has
 // fully retired; each kernel's first instruction waits until that predecessor has completed and its

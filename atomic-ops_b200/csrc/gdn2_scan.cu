@@ -169,8 +169,7 @@ cudaError_t launch_scan(const ScanParams& sp, int BH, cudaStream_t st) {
   // eagerly, it is dispatched ahead of the other groups' pending chunk-kernel CTAs (measured: the
   // un-graphed fwd+bwd step of B4 H6 L2048 fp32 0.994 against 1.022 ms); captured into a CUDA graph
   // the same priority made the replayed step 3 % slower, so captured launches keep the default.
-  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-  const bool urgent = cudaStreamIsCapturing(st, &cap) == cudaSuccess && cap == cudaStreamCaptureStatusNone;
+  const bool urgent = stream_eager(st);
   e = launch_pdl_prio(scan_kernel, (unsigned)(BH * (kD / kDV)), kThreads, kScanSmem, st, urgent, sp);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
