@@ -99,17 +99,13 @@ __device__ __forceinline__ void staged_sync() {
   __syncthreads();
 }
 
+// The MMA-completion barrier of a CTA and the parity of its next phase.  Every commit to it is
+// preceded by a CTA barrier that all its waiters pass only after their previous wait, so no waiter
+// can fall a whole phase behind.
 struct MmaBar {
   uint64_t* bar;
   uint32_t phase;
   unsigned* status;
-  __device__ __forceinline__ void commit_wait() {
-    if (threadIdx.x == 0) mma_commit(bar);
-    __syncwarp();
-    mbar_wait(bar, phase, status);
-    phase ^= 1u;
-    tc_fence_after();
-  }
 };
 
 // Element size in bytes and K elements per 128-byte slice.
