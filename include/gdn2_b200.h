@@ -127,7 +127,11 @@ gdn2_status gdn2_bwd(const gdn2_desc* desc, const void* q, const void* k, const 
  * under capture before that runs as one group).  A call whose B*H*(L/128) chunk-heads fit in one
  * wave of the GPU's multiprocessors runs as one group whatever n is.  Results do not depend on the
  * grouping.  n is clamped to [1, 8]; the initial value is the environment's GDN2_STREAMS, else 6.
- * Returns the previous value. */
+ * Returns the previous value.
+ * Scheduling: the state-scan launches of a call that is not being captured carry the device's
+ * greatest launch priority (they are the short sequential links of each group's chain), so their
+ * CTAs are dispatched ahead of pending CTAs of lower-priority streams, the caller's other work on
+ * the device included; launches under capture keep the default priority. */
 int32_t gdn2_set_batch_groups(int32_t n);
 int32_t gdn2_get_batch_groups(void);
 
