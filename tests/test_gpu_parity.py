@@ -73,6 +73,16 @@ def test_forward_backward_vs_oracle(mode):
     _compare(_run_op(cfg, xs, h0), _run_oracle(cfg, xs, h0), tol)
 
 
+@pytest.mark.parametrize("mode", ["fp32", "bf16x3"])
+def test_single_chunk_without_h0(mode):
+    """Edge shape: L = bt (one chunk per head, so each state scan runs a single step and loads a
+    single transition image), an odd head count, and h0 = None (zero initial state, no dh0)."""
+    kw, tol = MODES[mode]
+    cfg = make_cfg(wy_eps=0.0, **kw)
+    xs, _ = O.bench_inputs(1, 3, 128, D, 11)
+    _compare(_run_op(cfg, xs, None), _run_oracle(cfg, xs, None), tol, NAMES[:-1])
+
+
 def test_bf16_inputs_bf16_grads():
     """bf16 inputs -> bf16 gradients (test_t5_grad_vs_reference.py:51-59); oracle fed the
     bf16-rounded inputs upcast."""
